@@ -1,0 +1,466 @@
+#!/usr/bin/env python3
+"""Benchmark: WeLMv4 in-place partial RoPE, ordinary prefill M=16384, BF16.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+One step = one launch of the op over one batch: Q bf16 [16384, 6, 256] and
+K bf16 [16384, 1, 256] rotated in place at positions 0..16383 with an FP32
+cos/sin cache [16384, 64] (rotary base 1e4), seeded N(0,1) synthetic data.
+
+* ``value``: whole-job throughput in GB/s of ALGORITHMIC bytes (2056 B per
+  token: Q 6 and K 1 rope slices read + written, one 256-B cos/sin row and an
+  8-B position per token), with inputs resident in HBM.  K launches are
+  replayed from a CUDA graph over 8 rotating buffer sets (270 MB touched
+  between reuses, > 126 MB L2) and timed with CUDA events on the launching
+  stream; multi-GPU runs take the max time over ranks.
+* ``e2e``: the same metric through the public API with pinned HOST buffers:
+  each step copies Q, K and positions host->device, calls
+  ``welmv4_inplace_rope_npu`` and copies Q and K back, all inside the timed
+  region.
+* ``roofline``: the op kernel's achieved GB/s (algorithmic bytes per launch
+  over the average launch time of the graph-replayed region) against the
+  measured HBM copy peak.
+* ``cpu_baseline`` (rank 0, N=1 only): the reference's CPU algorithm (the
+  oracle port of its torch path) on this host's cores, same workload.
+
+``--impl reference`` times the reference's CPU implementation alone (rank 0;
+other ranks exit 0).  Multi-GPU runs (torchrun) shard requests: each rank
+rotates its own 16384-token request (weak scaling); there is no collective
+in the timed region.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+REPO = Path(__file__).resolve().parent
+if str(REPO) not in sys.path:
+    sys.path.insert(0, str(REPO))
+
+METRIC = "µs/launch and achieved HBM GB/s (% of roofline) for M=16384 BF16 prefill RoPE"
+TOKENS = 16384
+BUFFER_SETS = 8
+GRAPH_LAUNCHES = 64
+FALLBACK_HBM_GBS = 6650.0
+PROFILE_SUMMARY = REPO / "profiles" / "rope_ordinary_prefill_m16384.md"
+REFERENCE_BUDGET_S = 60.0
+
+
+def algorithmic_bytes(tokens: int) -> int:
+    return 2056 * tokens
+
+
+def workload_config(world: int) -> dict:
+    return {
+        "workload": "ordinary prefill in-place partial RoPE, M=16384 tokens per GPU, "
+                    "Q bf16 [16384,6,256], K bf16 [16384,1,256], positions 0..16383, "
+                    "cos/sin fp32 [16384,64] base 1e4, rope lanes 192..255",
+        "tokens_per_gpu": TOKENS,
+        "global_tokens": TOKENS * world,
+        "head_dim": 256,
+        "rope_dim": 64,
+        "q_heads": 6,
+        "k_heads": 1,
+        "parallelism": f"request-sharded dp{world}",
+        "l2_policy": f"{BUFFER_SETS} rotating buffer sets (~{BUFFER_SETS * algorithmic_bytes(TOKENS) / 1e6:.0f} MB "
+                     "touched between reuses > 126 MB L2)",
+        "bytes_per_launch": algorithmic_bytes(TOKENS),
+    }
+
+
+# ---------------------------------------------------------------------------
+# Distributed plumbing.
+# ---------------------------------------------------------------------------
+def dist_env() -> tuple[int, int, int]:
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def init_dist(world: int, local_rank: int):
+    if world <= 1:
+        return None
+    import datetime
+
+    import torch.distributed as dist
+
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", local_rank))
+    return dist
+
+
+def max_over_ranks(dist, value: float, device) -> float:
+    if dist is None:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(dist, device) -> None:
+    if dist is not None:
+        dist.barrier(device_ids=[device.index])
+    torch.cuda.synchronize(device)
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling (NVML reads only; no setting is changed).
+# ---------------------------------------------------------------------------
+REASON_BITS = {
+    0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+    0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+    0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+}
+
+
+class ClockSampler:
+    def __init__(self, device_index: int, period_s: float = 0.02):
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+            index = int(visible.split(",")[device_index]) if visible else device_index
+            self._nvml = pynvml
+            self._handle = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+        except Exception:  # noqa: BLE001 - clocks are reported as unavailable
+            self._nvml = None
+        self.period = period_s
+
+    def _run(self):
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self._handle, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
+                self.samples.append((mhz, reasons))
+            except Exception:  # noqa: BLE001
+                pass
+            self._stop.wait(self.period)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self) -> dict:
+        if self._nvml is None or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        busy = [s for s in self.samples if not s[1] & 0x1] or self.samples
+        reasons = 0
+        for _, r in busy:
+            reasons |= r
+        return {
+            "sm_mhz": statistics.median(m for m, _ in busy),
+            "sm_max_mhz": self.max_mhz,
+            "reasons": [name for bit, name in REASON_BITS.items() if reasons & bit and bit != 0x1],
+            "samples": len(busy),
+        }
+
+
+# ---------------------------------------------------------------------------
+# Peaks and profile figures.
+# ---------------------------------------------------------------------------
+def hbm_peak() -> tuple[float, str]:
+    path = REPO / "MEASURED_PEAKS.json"
+    try:
+        value = float(json.loads(path.read_text())["hbm_gbs"])
+        return value, "measured"
+    except Exception:  # noqa: BLE001
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic() -> int | None:
+    """DRAM bytes per launch (read + write) from the committed ncu summary."""
+    try:
+        for line in PROFILE_SUMMARY.read_text().splitlines():
+            if line.strip().startswith("traffic_bytes_per_launch:"):
+                return int(float(line.split(":", 1)[1].strip().split()[0]))
+    except Exception:  # noqa: BLE001
+        return None
+    return None
+
+
+# ---------------------------------------------------------------------------
+# CPU leg (the reference's CPU algorithm, via the oracle port).
+# ---------------------------------------------------------------------------
+def cpu_reference_time(inputs, runs: int, warmup: int = 1) -> tuple[list[float], int]:
+    from oracle import rope_oracle
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    times = []
+    for i in range(warmup + runs):
+        t0 = time.perf_counter()
+        rope_oracle.reference_outputs(inputs.query, inputs.key, inputs.positions, None, inputs.cache)
+        dt = time.perf_counter() - t0
+        if i >= warmup:
+            times.append(dt)
+    return times, threads
+
+
+def run_reference_arm(args) -> int:
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    from testfiles_b200 import workloads
+
+    case = workloads.Case("bench_prefill_m16384", "prefill", TOKENS, flavour="baseline")
+    inputs = workloads.make_inputs(case, "cpu")
+    # Each step is a bounded sample of the workload: the first `sample`
+    # tokens (a multiple of 64), sized so all warm-up + timed steps take about
+    # REFERENCE_BUDGET_S seconds of CPU time.
+    full, threads = cpu_reference_time(inputs, runs=1, warmup=1)
+    budget = REFERENCE_BUDGET_S / (args.steps + args.warmup)
+    sample = int(min(TOKENS, max(64, TOKENS * budget / full[0])) // 64 * 64)
+    part = workloads.Inputs(inputs.query[:sample], inputs.key[:sample], inputs.positions[:sample], inputs.cache)
+    times, threads = cpu_reference_time(part, runs=args.steps, warmup=max(0, args.warmup))
+    per_step = statistics.mean(times)
+    gbs = algorithmic_bytes(sample) / per_step / 1e9
+    per_launch_us = per_step * 1e6 * TOKENS / sample
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(gbs, 3),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(per_step * 1e3, 4),
+        "us_per_launch": round(per_launch_us, 2),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) bf16 Q/K, positions 0..M-1)",
+        "config": workload_config(1),
+        "cpu_baseline": {
+            "value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"first {sample} of 16384 tokens per step (reference torch CPU path restated), "
+                      f"{args.steps} steps after {args.warmup} warm-up, mean; us_per_launch scaled to M=16384",
+        },
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# GPU arm.
+# ---------------------------------------------------------------------------
+def run_b200_arm(args) -> int:
+    import testfiles_b200 as welm
+    from testfiles_b200 import sharding, workloads
+
+    rank, world, local_rank = dist_env()
+    if world != args.gpus and world > 1:
+        print(f"warning: WORLD_SIZE={world} but --gpus {args.gpus}", file=sys.stderr)
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    dist = init_dist(world, local_rank)
+
+    # Weak scaling: the global batch is one 16384-token request per rank,
+    # sharded by whole requests (no exchange on the hot path).
+    shards = sharding.shard_requests([TOKENS] * world, world)
+    r0, r1 = shards[rank]
+    local = sharding.local_batch([TOKENS] * world, (r0, r1))
+    n_tokens = local.n_tokens
+    assert n_tokens == TOKENS
+
+    case = workloads.Case("bench_prefill_m16384", "prefill", n_tokens, flavour="baseline")
+    host = workloads.make_inputs(case, "cpu")
+    cache = host.cache.to(device)
+    positions = host.positions.to(device)
+    sets = []
+    for _ in range(BUFFER_SETS):
+        sets.append((host.query.to(device), host.key.to(device), positions.clone(), cache.clone()))
+    launches = 0
+
+    def step(i: int) -> None:
+        q, k, p, c = sets[i % BUFFER_SETS]
+        welm.welmv4_inplace_rope_npu(q, k, p, c)
+
+    stream = torch.cuda.current_stream(device)
+    sampler = ClockSampler(device.index)
+    with sampler:
+        # Eager warm-up (also loads the kernels before any capture).
+        for i in range(max(3, args.warmup)):
+            step(i)
+        torch.cuda.synchronize(device)
+
+        # Capture the timed launches: `body` holds GRAPH_LAUNCHES launches
+        # cycling through the buffer sets, `tail` the remainder, so exactly
+        # K launches run in the timed region.
+        def capture(count: int):
+            if count == 0:
+                return None
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for i in range(count):
+                    step(i)
+            return g
+
+        body = capture(GRAPH_LAUNCHES)
+        reps, rem = divmod(args.steps, GRAPH_LAUNCHES)
+        tail = capture(rem)
+        for _ in range(3):
+            body.replay()
+        torch.cuda.synchronize(device)
+
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier(dist, device)
+        start.record(stream)
+        for _ in range(reps):
+            body.replay()
+        if tail is not None:
+            tail.replay()
+        end.record(stream)
+        barrier(dist, device)
+        launches += args.steps
+        elapsed_ms = max_over_ranks(dist, start.elapsed_time(end), device)
+
+        # End to end through the public API with pinned host buffers.
+        e2e_steps = max(1, min(args.steps, args.e2e_steps))
+        h_q = host.query.pin_memory()
+        h_k = host.key.pin_memory()
+        h_p = host.positions.pin_memory()
+        o_q = torch.empty_like(h_q).pin_memory()
+        o_k = torch.empty_like(h_k).pin_memory()
+        d_q, d_k, d_p = torch.empty_like(sets[0][0]), torch.empty_like(sets[0][1]), torch.empty_like(positions)
+
+        def e2e_step() -> None:
+            d_q.copy_(h_q, non_blocking=True)
+            d_k.copy_(h_k, non_blocking=True)
+            d_p.copy_(h_p, non_blocking=True)
+            welm.welmv4_inplace_rope_npu(d_q, d_k, d_p, cache)
+            o_q.copy_(d_q, non_blocking=True)
+            o_k.copy_(d_k, non_blocking=True)
+
+        for _ in range(3):
+            e2e_step()
+        torch.cuda.synchronize(device)
+        barrier(dist, device)
+        e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e_start.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e_end.record(stream)
+        barrier(dist, device)
+        e2e_ms = max_over_ranks(dist, e_start.elapsed_time(e_end), device)
+        launches_e2e = e2e_steps
+    torch.cuda.synchronize(device)
+    del body, tail
+
+    per_step_s = elapsed_ms / 1e3 / args.steps
+    total_bytes = algorithmic_bytes(TOKENS) * world
+    value = total_bytes / per_step_s / 1e9
+    per_launch_gbs = algorithmic_bytes(TOKENS) / per_step_s / 1e9
+    peak, peak_kind = hbm_peak()
+    e2e_per_step = e2e_ms / 1e3 / e2e_steps
+    h2d = host.query.numel() * 2 + host.key.numel() * 2 + host.positions.numel() * 8
+    d2h = host.query.numel() * 2 + host.key.numel() * 2
+
+    line = None
+    if rank == 0:
+        cpu = None
+        if world == 1:
+            times, threads = cpu_reference_time(host, runs=5)
+            cpu_t = statistics.median(times)
+            cpu = {
+                "value": round(algorithmic_bytes(TOKENS) / cpu_t / 1e9, 3),
+                "unit": "GB/s",
+                "cores": threads,
+                "kind": "port",
+                "sample": "full M=16384 prefill (reference torch CPU path restated), median of 5 after 1 warm-up; "
+                          f"{cpu_t * 1e3:.2f} ms/launch",
+            }
+        line = {
+            "impl": "b200",
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(per_step_s * 1e3, 6),
+            "us_per_launch": round(per_step_s * 1e6, 3),
+            "tokens_per_s": round(TOKENS * world / per_step_s, 1),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "math": "f32 (separate mul/sub/add roundings, one RNE to bf16)",
+            "data": "synthetic (seeded N(0,1) bf16 Q/K, positions 0..M-1)",
+            "config": workload_config(world),
+            "roofline": {
+                "bound": "hbm",
+                "achieved": round(per_launch_gbs, 2),
+                "peak": peak,
+                "unit": "GB/s",
+                "frac": round(per_launch_gbs / peak, 4),
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                else "fallback 6.65 TB/s",
+                "frac_of_8tbs_spec": round(per_launch_gbs / 8000.0, 4),
+                "traffic": profiled_traffic(),
+                "kernel": "rope_ordinary_kernel<vec,contiguous>",
+                "bytes_per_launch": algorithmic_bytes(TOKENS),
+            },
+            "cpu_baseline": cpu,
+            "e2e": {
+                "value": round(total_bytes / e2e_per_step / 1e9, 3),
+                "unit": "GB/s",
+                "us_per_step": round(e2e_per_step * 1e6, 2),
+                "steps": e2e_steps,
+                "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
+                "api": "testfiles_b200.welmv4_inplace_rope_npu (pinned host buffers, copies in the timed region)",
+            },
+            "clocks": sampler.summary(),
+            "gpu_launches": launches,
+            "gpu_launches_e2e": launches_e2e,
+        }
+    if dist is not None:
+        dist.barrier(device_ids=[device.index])
+        dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def main() -> int:
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=20000)
+    parser.add_argument("--warmup", type=int, default=50)
+    parser.add_argument("--e2e-steps", type=int, default=100)
+    parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    args = parser.parse_args()
+    if args.steps <= 0:
+        raise SystemExit("--steps must be positive")
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device (the op has no CPU path)")
+    return run_b200_arm(args)
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,154 @@
+/*
+ * welm_rope.h — C ABI of the B200 (sm_100a) WeLMv4 in-place partial RoPE.
+ *
+ * The op rotates the LAST 64 lanes (192..255) of every 256-lane BF16 head of
+ * Q [rows, 6, 256] and K [N, 1, 256] in place, with an FP32 cos/sin cache
+ * [max_position, 64] (cos in columns 0..31, sin in 32..63) gathered by int64
+ * position:
+ *     x1 = head[192..223], x2 = head[224..255], c = cache[p, 0..31], s = cache[p, 32..63]
+ *     head[192..223] = bf16(x1*c - x2*s)      head[224..255] = bf16(x1*s + x2*c)
+ * with each product, the difference and the sum rounded separately in FP32
+ * (no fused multiply-add) and one round-to-nearest-even to BF16.  Lanes
+ * 0..191 are never written.
+ *
+ * Each entry point replaces one launch site of the reference benchmark
+ * (bench_welmv4_inplace_rope_npu.py); the argument list
+ * keeps the reference kernel's runtime arguments in the same order, as plain
+ * pointers and 64-bit integers, and adds only `max_position`, an optional
+ * device status word and the stream.
+ *
+ * Conventions for every entry point:
+ *   - pointers are device pointers (except the *_host functions);
+ *   - token strides are in ELEMENTS (torch `tensor.stride(0)`); the six Q
+ *     heads of a token are contiguous (head stride 256 elements);
+ *   - `stream` is a cudaStream_t / CUstream handle (NULL = legacy default
+ *     stream) of the current device;
+ *   - the call only enqueues work: it never synchronises, never allocates,
+ *     never throws and never aborts; it returns a welm_rope_status code;
+ *   - `device_status` (may be NULL) is a caller-owned int32 in device memory;
+ *     when non-NULL the kernel ORs WELM_ROPE_DEV_* bits into it for tokens or
+ *     rows it skipped because an index was out of range.  Out-of-range tokens
+ *     are always skipped (left unmodified), never read out of bounds.
+ *   - 16-byte aligned bases and token strides that are multiples of 8
+ *     elements take the vectorised path; anything else takes a scalar path
+ *     with identical results.
+ */
+#ifndef WELM_ROPE_H_
+#define WELM_ROPE_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Host-side return codes. */
+typedef enum welm_rope_status {
+  WELM_ROPE_OK = 0,
+  WELM_ROPE_ERR_NULL_POINTER = 1, /* a required pointer is NULL                   */
+  WELM_ROPE_ERR_BAD_MODE = 2,     /* has_segments not in {0,1}, or mode misuse    */
+  WELM_ROPE_ERR_BAD_SIZE = 3,     /* negative or too large N / BS / tiles / P     */
+  WELM_ROPE_ERR_BAD_STRIDE = 4,   /* token stride makes rows overlap              */
+  WELM_ROPE_ERR_CAPACITY = 5,     /* output buffer too small (tile builder)       */
+  WELM_ROPE_ERR_CUDA = 6          /* the CUDA runtime refused the launch          */
+} welm_rope_status;
+
+/* Device-side status bits (ORed into *device_status when it is non-NULL). */
+#define WELM_ROPE_DEV_BAD_POSITION 1   /* positions[t] outside [0, max_position)        */
+#define WELM_ROPE_DEV_BAD_LAST_INDEX 2 /* last_index[b] outside [0, N)                  */
+#define WELM_ROPE_DEV_BAD_TILE 4       /* tile start/end outside [0, N], or > 64 tokens */
+#define WELM_ROPE_DEV_BAD_LENGTH 8     /* negative request length (tile builder)        */
+
+/* Fixed model contract (bench_welmv4_inplace_rope_npu.py:48-58): head_dim 256, rope_dim 64, 6 Q heads,
+ * 1 K head, 64-token work tiles. */
+#define WELM_ROPE_HEAD_DIM 256
+#define WELM_ROPE_ROPE_DIM 64
+#define WELM_ROPE_NUM_Q_HEADS 6
+#define WELM_ROPE_TILE_TOKENS 64
+
+/*
+ * Ordinary prefill / decode: rotate K row t (1 head) and Q row t (6 heads)
+ * at positions[t] for every token t covered by the work tiles.
+ *
+ * Replaces `_candidate_welmv4_inplace_rope_prefill_kernel[(grid,)](q, k,
+ * positions, cache, segment_tile_starts_or_placeholder, num_work_tiles, N,
+ * q_token_stride, k_token_stride, has_segments)` (bench_welmv4_inplace_rope_npu.py:670-690, bound at
+ * bench_welmv4_inplace_rope_npu.py:1267-1322 and 1324-1388) and the per-token decode kernels
+ * (bench_welmv4_inplace_rope_npu.py:326-405, 443-526) called with last_index = None.
+ *
+ *   has_segments == 0: tile i covers tokens [64 i, min(64 i + 64, N)) for
+ *       i < num_work_tiles (the reference passes ceil(N/64)); the
+ *       segment_tile_starts pointer is not dereferenced and may be NULL.
+ *   has_segments == 1: tile i covers [starts[i], starts[i] + min(64,
+ *       starts[i+1] - starts[i])) for i < num_work_tiles; N bounds the tokens.
+ * Positions are gathered per token, so no contiguity inside a tile is needed.
+ */
+int welm_rope_ordinary(void* q, void* k, const int64_t* positions,
+                       const float* cos_sin_cache,
+                       const int32_t* segment_tile_starts,
+                       int64_t num_work_tiles, int64_t n_tokens,
+                       int64_t q_token_stride, int64_t k_token_stride,
+                       int64_t has_segments, int64_t max_position,
+                       int32_t* device_status, void* stream);
+
+/*
+ * KV-mirror prefill: Q holds BS rows (one per request); row b is rotated at
+ * positions[last_index[b]].  K holds N rows, each rotated at positions[t]
+ * for the tokens covered by the work tiles (same tile rules as above).
+ *
+ * Replaces `_candidate_welmv4_inplace_rope_mirror_prefill_kernel[(grid,)](q,
+ * k, positions, cache, last_index, segment_tile_starts_or_placeholder,
+ * num_work_tiles, N, BS, q_token_stride, k_token_stride, has_segments)`
+ * (bench_welmv4_inplace_rope_npu.py:808-831, bound at bench_welmv4_inplace_rope_npu.py:1176-1205 and 1207-1265) and the
+ * frozen per-token kernel called with a last_index tensor (bench_welmv4_inplace_rope_npu.py:371-395).
+ */
+int welm_rope_mirror(void* q, void* k, const int64_t* positions,
+                     const float* cos_sin_cache, const int64_t* last_index,
+                     const int32_t* segment_tile_starts, int64_t num_work_tiles,
+                     int64_t n_tokens, int64_t batch_size,
+                     int64_t q_token_stride, int64_t k_token_stride,
+                     int64_t has_segments, int64_t max_position,
+                     int32_t* device_status, void* stream);
+
+/*
+ * Segmented 64-token tile-boundary builder on the device.  For request r of
+ * length len_r starting at token off_r it emits off_r, off_r+64, ... (< off_r
+ * + len_r), then the final total N: int32 starts[T+1], T = sum ceil(len_r/64).
+ * Tiles never cross a request boundary.  Optionally also writes
+ * last_index[r] = off_r + len_r - 1 (int64).  *num_tiles_out (device int32)
+ * receives T; `capacity` is the number of int32 slots in `tile_starts`
+ * (T + 1 <= ceil(N/64) + BS + 1 always suffices); entries past capacity are
+ * not written and WELM_ROPE_DEV_BAD_TILE is raised.  Negative lengths count
+ * as 0 and raise WELM_ROPE_DEV_BAD_LENGTH.
+ *
+ * Replaces the host loop inside make_inputs (bench_welmv4_inplace_rope_npu.py:1439-1461) and
+ * make_last_index (bench_welmv4_inplace_rope_npu.py:1402-1424, segmented branch).
+ */
+int welm_rope_build_tiles(const int64_t* seq_lens, int64_t batch_size,
+                          int32_t* tile_starts, int64_t capacity,
+                          int32_t* num_tiles_out, int64_t* last_index_out,
+                          int32_t* device_status, void* stream);
+
+/*
+ * Host twins of the builder (plain host memory, no CUDA call).  count returns
+ * T in *num_tiles_out; build fills starts[0..T] (needs capacity >= T + 1) and,
+ * when last_index_out is non-NULL, last_index[0..BS).  Negative lengths are
+ * rejected with WELM_ROPE_ERR_BAD_SIZE.  Same reference lines as above.
+ */
+int welm_rope_count_tiles_host(const int64_t* seq_lens, int64_t batch_size,
+                               int64_t* num_tiles_out);
+int welm_rope_build_tiles_host(const int64_t* seq_lens, int64_t batch_size,
+                               int32_t* tile_starts, int64_t capacity,
+                               int64_t* num_tiles_out, int64_t* last_index_out);
+
+/* Human-readable name of a welm_rope_status code (static storage). */
+const char* welm_rope_status_string(int status);
+
+/* ABI version of this header: (major << 16) | minor. */
+int welm_rope_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WELM_ROPE_H_ */

@@ -1,0 +1,575 @@
+// welm_rope.cu — sm_100a kernels and C ABI for WeLMv4's in-place partial RoPE.
+//
+// Semantics follow the reference's oracle `apply_reference` /
+// `reference_outputs` (bench_welmv4_inplace_rope_npu.py:1489-1521): for every
+// rotated row, lanes 192..223 (x1) and 224..255 (x2) of each 256-lane head
+// become bf16(x1*c - x2*s) and bf16(x1*s + x2*c), where c and s are the cos and
+// sin halves of the FP32 cache row at the row's position.  Products, the
+// difference and the sum are each rounded in FP32 (__fmul_rn/__fsub_rn/
+// __fadd_rn: no FMA contraction), then one round-to-nearest-even to BF16,
+// exactly as the reference's separate torch elementwise ops round.
+//
+// Work decomposition (B200-first, not the reference's 56-program tile loop):
+//   * one work item = (row, part): a thread owns 8 lanes of x1 and the
+//     matching 8 lanes of x2 of every head of that row, i.e. two 16-byte
+//     vectors per head; 4 threads cover a row's 128-byte rope slice per head;
+//   * the thread loads its 8 cos + 8 sin values once (four 16-byte loads) and
+//     reuses them from registers for all heads of the row (7 for the ordinary
+//     op: 1 K + 6 Q), so each cache row crosses HBM once per token;
+//   * every data load of the row is issued before the position-dependent
+//     cache load, so the position -> cache dependency overlaps the data
+//     stream; the grid is sized so a whole prefill is resident in one wave.
+//   * 64-token work tiles are kept only as the segment / masking unit of the
+//     reference's contract; positions are gathered per token, so no
+//     contiguity inside a tile is assumed (bench_welmv4_inplace_rope_npu.py:714-715
+//     assumes it, the oracle does not).
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include <atomic>
+
+#include "welm_rope.h"
+
+namespace {
+
+constexpr int kHeadDim = WELM_ROPE_HEAD_DIM;        // 256 lanes per head
+constexpr int kRopeDim = WELM_ROPE_ROPE_DIM;        // 64 rotated lanes
+constexpr int kHalf = kRopeDim / 2;                 // 32: x1 / x2 width
+constexpr int kRopeLane0 = kHeadDim - kRopeDim;     // 192: first rotated lane
+constexpr int kQHeads = WELM_ROPE_NUM_Q_HEADS;      // 6
+constexpr int kTile = WELM_ROPE_TILE_TOKENS;        // 64
+constexpr int kLanes = 8;                           // x1 lanes owned by one thread
+constexpr int kParts = kHalf / kLanes;              // 4 threads per row slice
+constexpr int kPartShift = 2;                       // log2(kParts)
+constexpr int kBlock = 128;                         // threads per CTA
+constexpr int kMaxDevices = 64;
+
+static_assert(kParts == (1 << kPartShift), "part count must be a power of two");
+
+struct RopeArgs {
+  uint16_t* q;                 // BF16 bits
+  uint16_t* k;                 // BF16 bits
+  const int64_t* positions;    // [N]
+  const float* cache;          // [max_position, 64]
+  const int64_t* last_index;   // [BS] (mirror only)
+  const int32_t* tile_starts;  // [num_tiles + 1] (segmented only)
+  int64_t q_stride;            // elements between Q rows
+  int64_t k_stride;            // elements between K rows
+  int64_t n_tokens;            // K rows / positions length
+  int64_t max_position;        // cache rows
+  int32_t* status;             // optional device status word
+  int32_t q_items;             // Q-row items (mirror): BS * kParts
+  int32_t k_items;             // token items: tokens (or tile slots) * kParts
+};
+
+struct CosSin {
+  float c[kLanes];
+  float s[kLanes];
+};
+
+__device__ __forceinline__ void raise_status(int32_t* status, int bit) {
+  if (status != nullptr) atomicOr(status, bit);
+}
+
+// ---------------------------------------------------------------------------
+// Loads / stores.  kVec: 16-byte vectors (bases 16-byte aligned, strides a
+// multiple of 8 elements); otherwise 2-byte scalars with the same results.
+// ---------------------------------------------------------------------------
+template <bool kVec>
+struct Io;
+
+template <>
+struct Io<true> {
+  static __device__ __forceinline__ uint4 load8(const uint16_t* p) {
+    return *reinterpret_cast<const uint4*>(p);
+  }
+  static __device__ __forceinline__ void store8(uint16_t* p, const uint4& v) {
+    *reinterpret_cast<uint4*>(p) = v;
+  }
+  static __device__ __forceinline__ void load_cos_sin(const float* row, int part, CosSin& cs) {
+    const float4* c = reinterpret_cast<const float4*>(row + part * kLanes);
+    const float4* s = reinterpret_cast<const float4*>(row + kHalf + part * kLanes);
+    const float4 c0 = __ldg(c), c1 = __ldg(c + 1), s0 = __ldg(s), s1 = __ldg(s + 1);
+    cs.c[0] = c0.x; cs.c[1] = c0.y; cs.c[2] = c0.z; cs.c[3] = c0.w;
+    cs.c[4] = c1.x; cs.c[5] = c1.y; cs.c[6] = c1.z; cs.c[7] = c1.w;
+    cs.s[0] = s0.x; cs.s[1] = s0.y; cs.s[2] = s0.z; cs.s[3] = s0.w;
+    cs.s[4] = s1.x; cs.s[5] = s1.y; cs.s[6] = s1.z; cs.s[7] = s1.w;
+  }
+};
+
+template <>
+struct Io<false> {
+  static __device__ __forceinline__ uint4 load8(const uint16_t* p) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) w[i] = uint32_t(p[2 * i]) | (uint32_t(p[2 * i + 1]) << 16);
+    return make_uint4(w[0], w[1], w[2], w[3]);
+  }
+  static __device__ __forceinline__ void store8(uint16_t* p, const uint4& v) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      p[2 * i] = uint16_t(w[i] & 0xffffu);
+      p[2 * i + 1] = uint16_t(w[i] >> 16);
+    }
+  }
+  static __device__ __forceinline__ void load_cos_sin(const float* row, int part, CosSin& cs) {
+#pragma unroll
+    for (int i = 0; i < kLanes; ++i) {
+      cs.c[i] = __ldg(row + part * kLanes + i);
+      cs.s[i] = __ldg(row + kHalf + part * kLanes + i);
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------
+// Arithmetic: one rotated pair per lane, FP32 with separate roundings.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);  // RNE, lo in the low half
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// x1 (8 lanes) and x2 (the matching 8 lanes) are rotated in place.
+__device__ __forceinline__ void rotate8(uint4& x1, uint4& x2, const CosSin& cs) {
+  uint32_t a[4] = {x1.x, x1.y, x1.z, x1.w};
+  uint32_t b[4] = {x2.x, x2.y, x2.z, x2.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float a0 = bf16_lo(a[i]), a1 = bf16_hi(a[i]);
+    const float b0 = bf16_lo(b[i]), b1 = bf16_hi(b[i]);
+    const float c0 = cs.c[2 * i], c1 = cs.c[2 * i + 1];
+    const float s0 = cs.s[2 * i], s1 = cs.s[2 * i + 1];
+    const float o0 = __fsub_rn(__fmul_rn(a0, c0), __fmul_rn(b0, s0));
+    const float o1 = __fsub_rn(__fmul_rn(a1, c1), __fmul_rn(b1, s1));
+    const float p0 = __fadd_rn(__fmul_rn(a0, s0), __fmul_rn(b0, c0));
+    const float p1 = __fadd_rn(__fmul_rn(a1, s1), __fmul_rn(b1, c1));
+    a[i] = pack_bf16x2(o0, o1);
+    b[i] = pack_bf16x2(p0, p1);
+  }
+  x1 = make_uint4(a[0], a[1], a[2], a[3]);
+  x2 = make_uint4(b[0], b[1], b[2], b[3]);
+}
+
+// ---------------------------------------------------------------------------
+// Token resolution for the token-phase slot `slot` (one slot per token of a
+// dense range, or 64 slots per work tile when segmented).  Returns false when
+// the slot is empty (tile tail) or out of range (then a status bit is raised).
+// Tile semantics are the reference kernels' (bench_welmv4_inplace_rope_npu.py:
+// 700-718, 856-867): tile i covers [starts[i], starts[i] + min(64, len)).
+// ---------------------------------------------------------------------------
+template <bool kSegmented>
+__device__ __forceinline__ bool resolve_token(const RopeArgs& a, int slot, int part, int64_t& tok) {
+  if (!kSegmented) {
+    tok = slot;  // the host sized k_items to min(N, 64 * num_work_tiles)
+    return true;
+  }
+  const int tile = slot / kTile;
+  const int j = slot - tile * kTile;
+  const int64_t begin = __ldg(a.tile_starts + tile);
+  const int64_t end = __ldg(a.tile_starts + tile + 1);
+  int64_t count = end - begin;
+  if (j == 0 && part == 0 && (begin < 0 || end > a.n_tokens || count < 0 || count > kTile))
+    raise_status(a.status, WELM_ROPE_DEV_BAD_TILE);
+  if (count > kTile) count = kTile;
+  if (j >= count) return false;
+  tok = begin + j;
+  return tok >= 0 && tok < a.n_tokens;  // out-of-range tokens are skipped, never touched
+}
+
+// Rotates NH heads (head stride 256 lanes) of one row for one part.  All data
+// loads are issued before the position check and the cache gather.
+template <bool kVec, int NH>
+__device__ __forceinline__ void rotate_row(uint16_t* __restrict__ row, int64_t pos,
+                                           const RopeArgs& a, int part, int bad_bit) {
+  uint16_t* base = row + kRopeLane0 + part * kLanes;
+  uint4 x1[NH], x2[NH];
+#pragma unroll
+  for (int h = 0; h < NH; ++h) {
+    x1[h] = Io<kVec>::load8(base + h * kHeadDim);
+    x2[h] = Io<kVec>::load8(base + h * kHeadDim + kHalf);
+  }
+  if (pos < 0 || pos >= a.max_position) {
+    if (part == 0) raise_status(a.status, bad_bit);
+    return;
+  }
+  CosSin cs;
+  Io<kVec>::load_cos_sin(a.cache + pos * kRopeDim, part, cs);
+#pragma unroll
+  for (int h = 0; h < NH; ++h) {
+    rotate8(x1[h], x2[h], cs);
+    Io<kVec>::store8(base + h * kHeadDim, x1[h]);
+    Io<kVec>::store8(base + h * kHeadDim + kHalf, x2[h]);
+  }
+}
+
+// Ordinary prefill / decode: K head + 6 Q heads of token t at positions[t].
+// K and Q are fused into one 7-head row pass when both are 16-byte capable;
+// the cache row is loaded once for all seven heads.
+template <bool kVec, bool kSegmented>
+__global__ void __launch_bounds__(kBlock) rope_ordinary_kernel(const RopeArgs a) {
+  const int stride = gridDim.x * blockDim.x;
+  for (int item = blockIdx.x * blockDim.x + threadIdx.x; item < a.k_items; item += stride) {
+    const int part = item & (kParts - 1);
+    int64_t tok;
+    if (!resolve_token<kSegmented>(a, item >> kPartShift, part, tok)) continue;
+    const int64_t pos = __ldg(a.positions + tok);
+    uint16_t* kbase = a.k + tok * a.k_stride + kRopeLane0 + part * kLanes;
+    uint16_t* qbase = a.q + tok * a.q_stride + kRopeLane0 + part * kLanes;
+    uint4 kx1 = Io<kVec>::load8(kbase), kx2 = Io<kVec>::load8(kbase + kHalf);
+    uint4 qx1[kQHeads], qx2[kQHeads];
+#pragma unroll
+    for (int h = 0; h < kQHeads; ++h) {
+      qx1[h] = Io<kVec>::load8(qbase + h * kHeadDim);
+      qx2[h] = Io<kVec>::load8(qbase + h * kHeadDim + kHalf);
+    }
+    if (pos < 0 || pos >= a.max_position) {
+      if (part == 0) raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
+      continue;
+    }
+    CosSin cs;
+    Io<kVec>::load_cos_sin(a.cache + pos * kRopeDim, part, cs);
+    rotate8(kx1, kx2, cs);
+    Io<kVec>::store8(kbase, kx1);
+    Io<kVec>::store8(kbase + kHalf, kx2);
+#pragma unroll
+    for (int h = 0; h < kQHeads; ++h) {
+      rotate8(qx1[h], qx2[h], cs);
+      Io<kVec>::store8(qbase + h * kHeadDim, qx1[h]);
+      Io<kVec>::store8(qbase + h * kHeadDim + kHalf, qx2[h]);
+    }
+  }
+}
+
+// KV-mirror prefill.  Items [0, q_items) are the BS Q rows (6 heads at
+// positions[last_index[b]], bench_welmv4_inplace_rope_npu.py:839-854); items
+// [q_items, q_items + k_items) are the K tokens (1 head at positions[t],
+// bench_welmv4_inplace_rope_npu.py:856-919).  Q rows and K rows are disjoint
+// tensors, so the two phases need no ordering.
+template <bool kVec, bool kSegmented>
+__global__ void __launch_bounds__(kBlock) rope_mirror_kernel(const RopeArgs a) {
+  const int stride = gridDim.x * blockDim.x;
+  const int total = a.q_items + a.k_items;
+  for (int item = blockIdx.x * blockDim.x + threadIdx.x; item < total; item += stride) {
+    const int part = item & (kParts - 1);
+    if (item < a.q_items) {
+      const int b = item >> kPartShift;
+      uint16_t* row = a.q + int64_t(b) * a.q_stride;
+      const int64_t src = __ldg(a.last_index + b);
+      if (src < 0 || src >= a.n_tokens) {
+        if (part == 0) raise_status(a.status, WELM_ROPE_DEV_BAD_LAST_INDEX);
+        continue;
+      }
+      rotate_row<kVec, kQHeads>(row, __ldg(a.positions + src), a, part,
+                                WELM_ROPE_DEV_BAD_POSITION);
+    } else {
+      int64_t tok;
+      if (!resolve_token<kSegmented>(a, (item - a.q_items) >> kPartShift, part, tok)) continue;
+      rotate_row<kVec, 1>(a.k + tok * a.k_stride, __ldg(a.positions + tok), a, part,
+                          WELM_ROPE_DEV_BAD_POSITION);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Segmented tile-boundary builder: one CTA, requests processed in chunks of
+// kBuildThreads with a running carry (tokens, tiles).  Within a chunk the
+// per-request tile counts and lengths are scanned with warp shuffles, then the
+// chunk's tile starts are written cooperatively (each thread finds the
+// request of its tile by binary search over the chunk's inclusive scan).
+// ---------------------------------------------------------------------------
+constexpr int kBuildThreads = 1024;
+constexpr int kBuildWarps = kBuildThreads / 32;
+
+__device__ __forceinline__ void block_inclusive_scan2(int64_t& x, int64_t& y, int64_t* wx, int64_t* wy) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int64_t tx = __shfl_up_sync(0xffffffffu, x, d);
+    const int64_t ty = __shfl_up_sync(0xffffffffu, y, d);
+    if (lane >= d) { x += tx; y += ty; }
+  }
+  if (lane == 31) { wx[warp] = x; wy[warp] = y; }
+  __syncthreads();
+  if (warp == 0) {
+    int64_t vx = lane < kBuildWarps ? wx[lane] : 0;
+    int64_t vy = lane < kBuildWarps ? wy[lane] : 0;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int64_t tx = __shfl_up_sync(0xffffffffu, vx, d);
+      const int64_t ty = __shfl_up_sync(0xffffffffu, vy, d);
+      if (lane >= d) { vx += tx; vy += ty; }
+    }
+    if (lane < kBuildWarps) { wx[lane] = vx; wy[lane] = vy; }
+  }
+  __syncthreads();
+  if (warp > 0) { x += wx[warp - 1]; y += wy[warp - 1]; }
+}
+
+__global__ void __launch_bounds__(kBuildThreads)
+build_tiles_kernel(const int64_t* __restrict__ lens, int32_t bs, int32_t* __restrict__ starts,
+                   int64_t capacity, int32_t* __restrict__ num_tiles_out,
+                   int64_t* __restrict__ last_index_out, int32_t* status) {
+  __shared__ int64_t s_tok[kBuildThreads];   // inclusive token scan of the chunk
+  __shared__ int64_t s_tile[kBuildThreads];  // inclusive tile scan of the chunk
+  __shared__ int64_t wx[kBuildWarps], wy[kBuildWarps];
+  int64_t carry_tok = 0, carry_tile = 0;     // identical in every thread
+  for (int base = 0; base < bs; base += kBuildThreads) {
+    const int r = base + threadIdx.x;
+    int64_t len = 0;
+    if (r < bs) {
+      len = lens[r];
+      if (len < 0) {
+        raise_status(status, WELM_ROPE_DEV_BAD_LENGTH);
+        len = 0;
+      }
+    }
+    int64_t tok = len, tiles = (len + kTile - 1) / kTile;
+    block_inclusive_scan2(tok, tiles, wx, wy);
+    s_tok[threadIdx.x] = tok;
+    s_tile[threadIdx.x] = tiles;
+    if (r < bs && last_index_out != nullptr) last_index_out[r] = carry_tok + tok - 1;
+    __syncthreads();
+    const int chunk = min(kBuildThreads, bs - base);
+    const int64_t chunk_tiles = s_tile[chunk - 1];
+    for (int64_t t = threadIdx.x; t < chunk_tiles; t += kBuildThreads) {
+      int lo = 0, hi = chunk - 1;
+      while (lo < hi) {  // first request whose inclusive tile count exceeds t
+        const int mid = (lo + hi) >> 1;
+        if (s_tile[mid] > t) hi = mid; else lo = mid + 1;
+      }
+      const int64_t first_tile = lo > 0 ? s_tile[lo - 1] : 0;
+      const int64_t first_tok = lo > 0 ? s_tok[lo - 1] : 0;
+      const int64_t out = carry_tile + t;
+      const int64_t value = carry_tok + first_tok + (t - first_tile) * kTile;
+      if (out < capacity && value <= INT32_MAX) {
+        starts[out] = int32_t(value);
+      } else {
+        raise_status(status, WELM_ROPE_DEV_BAD_TILE);
+      }
+    }
+    carry_tok += s_tok[chunk - 1];
+    carry_tile += chunk_tiles;
+    __syncthreads();  // the next chunk overwrites s_tok / s_tile
+  }
+  if (threadIdx.x == 0) {
+    if (carry_tile < capacity && carry_tok <= INT32_MAX) {
+      starts[carry_tile] = int32_t(carry_tok);
+    } else {
+      raise_status(status, WELM_ROPE_DEV_BAD_TILE);
+    }
+    *num_tiles_out = carry_tile <= INT32_MAX ? int32_t(carry_tile) : -1;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side.
+// ---------------------------------------------------------------------------
+constexpr int64_t kMaxItems = int64_t(1) << 30;  // item indices stay in int32
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int current_sm_count() {
+  static std::atomic<int> cache[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return 0;
+  if (dev < kMaxDevices) {
+    const int v = cache[dev].load(std::memory_order_relaxed);
+    if (v > 0) return v;
+  }
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  if (dev < kMaxDevices) cache[dev].store(sms, std::memory_order_relaxed);
+  return sms;
+}
+
+// Grid for `items` work items: enough CTAs for one item per thread, capped at
+// what the device keeps resident (16 CTAs of 128 threads per SM, the
+// register-limited residency of these kernels) so the grid-stride loop covers
+// larger inputs.
+unsigned grid_for(int64_t items) {
+  const int sms = current_sm_count();
+  const int64_t need = (items + kBlock - 1) / kBlock;
+  const int64_t cap = sms > 0 ? int64_t(sms) * 16 : need;
+  return unsigned(need < cap ? need : cap);
+}
+
+int launch_status() {
+  return cudaGetLastError() == cudaSuccess ? WELM_ROPE_OK : WELM_ROPE_ERR_CUDA;
+}
+
+template <bool kVec, bool kSegmented>
+void launch_ordinary(const RopeArgs& a, cudaStream_t stream) {
+  rope_ordinary_kernel<kVec, kSegmented><<<grid_for(a.k_items), kBlock, 0, stream>>>(a);
+}
+
+template <bool kVec, bool kSegmented>
+void launch_mirror(const RopeArgs& a, cudaStream_t stream) {
+  rope_mirror_kernel<kVec, kSegmented>
+      <<<grid_for(int64_t(a.q_items) + a.k_items), kBlock, 0, stream>>>(a);
+}
+
+// Token-phase slot count shared by both ops (the reference's tile loops).
+int64_t token_slots(int64_t has_segments, int64_t num_work_tiles, int64_t n_tokens) {
+  if (has_segments) return num_work_tiles * kTile;
+  const int64_t covered = num_work_tiles * kTile;
+  return covered < n_tokens ? covered : n_tokens;
+}
+
+}  // namespace
+
+extern "C" {
+
+int welm_rope_abi_version(void) { return (1 << 16) | 0; }
+
+const char* welm_rope_status_string(int status) {
+  switch (status) {
+    case WELM_ROPE_OK: return "ok";
+    case WELM_ROPE_ERR_NULL_POINTER: return "a required pointer is NULL";
+    case WELM_ROPE_ERR_BAD_MODE: return "has_segments must be 0 or 1 (segmented mode needs segment_tile_starts)";
+    case WELM_ROPE_ERR_BAD_SIZE: return "negative or too large size argument";
+    case WELM_ROPE_ERR_BAD_STRIDE: return "token stride makes rows overlap";
+    case WELM_ROPE_ERR_CAPACITY: return "output buffer too small";
+    case WELM_ROPE_ERR_CUDA: return "CUDA launch failed";
+    default: return "unknown welm_rope status";
+  }
+}
+
+int welm_rope_ordinary(void* q, void* k, const int64_t* positions, const float* cos_sin_cache,
+                       const int32_t* segment_tile_starts, int64_t num_work_tiles,
+                       int64_t n_tokens, int64_t q_token_stride, int64_t k_token_stride,
+                       int64_t has_segments, int64_t max_position, int32_t* device_status,
+                       void* stream) {
+  if (has_segments != 0 && has_segments != 1) return WELM_ROPE_ERR_BAD_MODE;
+  if (num_work_tiles < 0 || n_tokens < 0 || max_position < 0) return WELM_ROPE_ERR_BAD_SIZE;
+  const int64_t slots = token_slots(has_segments, num_work_tiles, n_tokens);
+  if (slots > kMaxItems / kParts) return WELM_ROPE_ERR_BAD_SIZE;
+  if (slots == 0 || n_tokens == 0) return WELM_ROPE_OK;  // nothing to rotate
+  if (!q || !k || !positions || !cos_sin_cache) return WELM_ROPE_ERR_NULL_POINTER;
+  if (has_segments && !segment_tile_starts) return WELM_ROPE_ERR_NULL_POINTER;
+  if (n_tokens > 1 && (q_token_stride < kQHeads * kHeadDim || k_token_stride < kHeadDim))
+    return WELM_ROPE_ERR_BAD_STRIDE;
+
+  RopeArgs a{};
+  a.q = static_cast<uint16_t*>(q);
+  a.k = static_cast<uint16_t*>(k);
+  a.positions = positions;
+  a.cache = cos_sin_cache;
+  a.tile_starts = segment_tile_starts;
+  a.q_stride = q_token_stride;
+  a.k_stride = k_token_stride;
+  a.n_tokens = n_tokens;
+  a.max_position = max_position;
+  a.status = device_status;
+  a.k_items = int32_t(slots * kParts);
+  const bool vec = aligned16(q) && aligned16(k) && aligned16(cos_sin_cache) &&
+                   (n_tokens <= 1 || (q_token_stride % 8 == 0 && k_token_stride % 8 == 0));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (vec) {
+    if (has_segments) launch_ordinary<true, true>(a, s); else launch_ordinary<true, false>(a, s);
+  } else {
+    if (has_segments) launch_ordinary<false, true>(a, s); else launch_ordinary<false, false>(a, s);
+  }
+  return launch_status();
+}
+
+int welm_rope_mirror(void* q, void* k, const int64_t* positions, const float* cos_sin_cache,
+                     const int64_t* last_index, const int32_t* segment_tile_starts,
+                     int64_t num_work_tiles, int64_t n_tokens, int64_t batch_size,
+                     int64_t q_token_stride, int64_t k_token_stride, int64_t has_segments,
+                     int64_t max_position, int32_t* device_status, void* stream) {
+  if (has_segments != 0 && has_segments != 1) return WELM_ROPE_ERR_BAD_MODE;
+  if (num_work_tiles < 0 || n_tokens < 0 || batch_size < 0 || max_position < 0)
+    return WELM_ROPE_ERR_BAD_SIZE;
+  const int64_t slots = n_tokens > 0 ? token_slots(has_segments, num_work_tiles, n_tokens) : 0;
+  const int64_t rows = n_tokens > 0 ? batch_size : 0;  // Q rows need a valid last_index target
+  if (slots > kMaxItems / kParts || rows > kMaxItems / kParts ||
+      (slots + rows) * kParts > kMaxItems)
+    return WELM_ROPE_ERR_BAD_SIZE;
+  if (slots == 0 && rows == 0) return WELM_ROPE_OK;
+  if (!q || !k || !positions || !cos_sin_cache || !last_index) return WELM_ROPE_ERR_NULL_POINTER;
+  if (has_segments && slots > 0 && !segment_tile_starts) return WELM_ROPE_ERR_NULL_POINTER;
+  if ((rows > 1 && q_token_stride < kQHeads * kHeadDim) || (n_tokens > 1 && k_token_stride < kHeadDim))
+    return WELM_ROPE_ERR_BAD_STRIDE;
+
+  RopeArgs a{};
+  a.q = static_cast<uint16_t*>(q);
+  a.k = static_cast<uint16_t*>(k);
+  a.positions = positions;
+  a.cache = cos_sin_cache;
+  a.last_index = last_index;
+  a.tile_starts = segment_tile_starts;
+  a.q_stride = q_token_stride;
+  a.k_stride = k_token_stride;
+  a.n_tokens = n_tokens;
+  a.max_position = max_position;
+  a.status = device_status;
+  a.q_items = int32_t(rows * kParts);
+  a.k_items = int32_t(slots * kParts);
+  const bool vec = aligned16(q) && aligned16(k) && aligned16(cos_sin_cache) &&
+                   (rows <= 1 || q_token_stride % 8 == 0) &&
+                   (n_tokens <= 1 || k_token_stride % 8 == 0);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (vec) {
+    if (has_segments) launch_mirror<true, true>(a, s); else launch_mirror<true, false>(a, s);
+  } else {
+    if (has_segments) launch_mirror<false, true>(a, s); else launch_mirror<false, false>(a, s);
+  }
+  return launch_status();
+}
+
+int welm_rope_build_tiles(const int64_t* seq_lens, int64_t batch_size, int32_t* tile_starts,
+                          int64_t capacity, int32_t* num_tiles_out, int64_t* last_index_out,
+                          int32_t* device_status, void* stream) {
+  if (batch_size < 0 || batch_size > INT32_MAX || capacity < 0) return WELM_ROPE_ERR_BAD_SIZE;
+  if (capacity < 1) return WELM_ROPE_ERR_CAPACITY;  // starts[T] always needs a slot
+  if (!tile_starts || !num_tiles_out || (batch_size > 0 && !seq_lens))
+    return WELM_ROPE_ERR_NULL_POINTER;
+  build_tiles_kernel<<<1, kBuildThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      seq_lens, int32_t(batch_size), tile_starts, capacity, num_tiles_out, last_index_out,
+      device_status);
+  return launch_status();
+}
+
+int welm_rope_count_tiles_host(const int64_t* seq_lens, int64_t batch_size,
+                               int64_t* num_tiles_out) {
+  if (batch_size < 0) return WELM_ROPE_ERR_BAD_SIZE;
+  if (!num_tiles_out || (batch_size > 0 && !seq_lens)) return WELM_ROPE_ERR_NULL_POINTER;
+  int64_t tiles = 0;
+  for (int64_t r = 0; r < batch_size; ++r) {
+    if (seq_lens[r] < 0) return WELM_ROPE_ERR_BAD_SIZE;
+    tiles += (seq_lens[r] + kTile - 1) / kTile;
+  }
+  *num_tiles_out = tiles;
+  return WELM_ROPE_OK;
+}
+
+int welm_rope_build_tiles_host(const int64_t* seq_lens, int64_t batch_size, int32_t* tile_starts,
+                               int64_t capacity, int64_t* num_tiles_out,
+                               int64_t* last_index_out) {
+  int64_t tiles = 0;
+  const int rc = welm_rope_count_tiles_host(seq_lens, batch_size, &tiles);
+  if (rc != WELM_ROPE_OK) return rc;
+  if (!tile_starts) return WELM_ROPE_ERR_NULL_POINTER;
+  if (capacity < tiles + 1) return WELM_ROPE_ERR_CAPACITY;
+  int64_t token = 0, t = 0;
+  for (int64_t r = 0; r < batch_size; ++r) {
+    for (int64_t off = 0; off < seq_lens[r]; off += kTile) {
+      if (token + off > INT32_MAX) return WELM_ROPE_ERR_BAD_SIZE;
+      tile_starts[t++] = int32_t(token + off);
+    }
+    token += seq_lens[r];
+    if (last_index_out) last_index_out[r] = token - 1;
+  }
+  if (token > INT32_MAX) return WELM_ROPE_ERR_BAD_SIZE;
+  tile_starts[t] = int32_t(token);
+  if (num_tiles_out) *num_tiles_out = tiles;
+  return WELM_ROPE_OK;
+}
+
+}  // extern "C"

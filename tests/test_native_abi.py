@@ -1,0 +1,146 @@
+"""CPU checks of the C ABI: the library loads, exports every declared symbol,
+validates arguments on the host before any CUDA call, and its host tile
+builder twin matches the reference's tables.  No kernel is launched here."""
+
+from __future__ import annotations
+
+import ctypes
+import random
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+from conftest import REPO
+from oracle import rope_oracle
+from testfiles_b200 import _native, build
+import testfiles_b200 as welm
+
+HEADER = REPO / "include" / "welm_rope.h"
+
+
+def declared_symbols() -> set[str]:
+    text = HEADER.read_text()
+    return set(re.findall(r"^\s*(?:int|const char\*)\s+(welm_rope_\w+)\s*\(", text, flags=re.M))
+
+
+def test_library_is_built_for_sm100a_only():
+    assert build.LIBRARY.exists(), "run python -m testfiles_b200.build"
+    assert "arch=compute_100a,code=sm_100a" in build.NVCC_FLAGS
+
+
+def test_every_declared_symbol_is_exported_and_bound():
+    symbols = declared_symbols()
+    assert symbols == set(_native.SIGNATURES), symbols ^ set(_native.SIGNATURES)
+    out = subprocess.run(["nm", "-D", "--defined-only", str(build.LIBRARY)], capture_output=True, text=True,
+                         check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if line.strip()}
+    assert symbols <= exported, symbols - exported
+    lib = _native.load()
+    for name in symbols:
+        assert getattr(lib, name) is not None
+
+
+def test_abi_version_and_status_strings():
+    lib = _native.load()
+    assert lib.welm_rope_abi_version() >> 16 == 1
+    for code in range(7):
+        assert _native.status_string(code)
+    assert _native.status_string(99) == "unknown welm_rope status"
+
+
+FAKE = 0x1000  # a non-NULL address; every call below is rejected before it is used
+
+
+def ordinary(**kw):
+    args = dict(q=FAKE, k=FAKE, positions=FAKE, cache=FAKE, starts=None, tiles=1, n=1, qs=1536, ks=256,
+                seg=0, maxpos=16, status=None, stream=None)
+    args.update(kw)
+    return _native.load().welm_rope_ordinary(
+        args["q"], args["k"], args["positions"], args["cache"], args["starts"], args["tiles"], args["n"],
+        args["qs"], args["ks"], args["seg"], args["maxpos"], args["status"], args["stream"])
+
+
+def mirror(**kw):
+    args = dict(q=FAKE, k=FAKE, positions=FAKE, cache=FAKE, last=FAKE, starts=None, tiles=1, n=1, bs=1,
+                qs=1536, ks=256, seg=0, maxpos=16, status=None, stream=None)
+    args.update(kw)
+    return _native.load().welm_rope_mirror(
+        args["q"], args["k"], args["positions"], args["cache"], args["last"], args["starts"], args["tiles"],
+        args["n"], args["bs"], args["qs"], args["ks"], args["seg"], args["maxpos"], args["status"],
+        args["stream"])
+
+
+def test_host_validation_ordinary():
+    assert ordinary(seg=2) == _native.ERR_BAD_MODE
+    assert ordinary(seg=-1) == _native.ERR_BAD_MODE
+    assert ordinary(n=-1) == _native.ERR_BAD_SIZE
+    assert ordinary(tiles=-3) == _native.ERR_BAD_SIZE
+    assert ordinary(maxpos=-1) == _native.ERR_BAD_SIZE
+    assert ordinary(n=1 << 40, tiles=1 << 34) == _native.ERR_BAD_SIZE
+    assert ordinary(q=None) == _native.ERR_NULL_POINTER
+    assert ordinary(cache=None) == _native.ERR_NULL_POINTER
+    assert ordinary(seg=1, starts=None) == _native.ERR_NULL_POINTER
+    assert ordinary(n=4, tiles=1, qs=1535) == _native.ERR_BAD_STRIDE
+    assert ordinary(n=4, tiles=1, ks=255) == _native.ERR_BAD_STRIDE
+    # zero work is a no-op that needs no pointers and launches nothing
+    assert ordinary(q=None, k=None, positions=None, cache=None, n=0) == _native.OK
+    assert ordinary(q=None, k=None, positions=None, cache=None, tiles=0) == _native.OK
+
+
+def test_host_validation_mirror():
+    assert mirror(seg=3) == _native.ERR_BAD_MODE
+    assert mirror(bs=-1) == _native.ERR_BAD_SIZE
+    assert mirror(last=None) == _native.ERR_NULL_POINTER
+    assert mirror(bs=2, qs=100) == _native.ERR_BAD_STRIDE
+    assert mirror(n=2, ks=8) == _native.ERR_BAD_STRIDE
+    assert mirror(seg=1, starts=None) == _native.ERR_NULL_POINTER
+    assert mirror(q=None, k=None, positions=None, cache=None, last=None, n=0, bs=0) == _native.OK
+
+
+def test_host_validation_device_builder():
+    lib = _native.load()
+    assert lib.welm_rope_build_tiles(FAKE, -1, FAKE, 8, FAKE, None, None, None) == _native.ERR_BAD_SIZE
+    assert lib.welm_rope_build_tiles(FAKE, 2, FAKE, 0, FAKE, None, None, None) == _native.ERR_CAPACITY
+    assert lib.welm_rope_build_tiles(None, 2, FAKE, 8, FAKE, None, None, None) == _native.ERR_NULL_POINTER
+    assert lib.welm_rope_build_tiles(FAKE, 2, None, 8, FAKE, None, None, None) == _native.ERR_NULL_POINTER
+    assert lib.welm_rope_build_tiles(FAKE, 2, FAKE, 8, None, None, None, None) == _native.ERR_NULL_POINTER
+
+
+def test_host_builder_matches_reference_tables(tile_tables):
+    for name, rec in tile_tables.items():
+        starts, tiles, last = welm.build_segment_tile_starts(rec["segment_lens"])
+        assert starts.tolist() == rec["segment_tile_starts"], name
+        assert tiles == len(rec["segment_tile_starts"]) - 1
+        if rec["last_index"] is not None:
+            assert last.tolist() == rec["last_index"], name
+
+
+def test_host_builder_random_lengths_match_oracle():
+    rng = random.Random(7)
+    for _ in range(200):
+        bs = rng.randint(0, 40)
+        lens = [rng.choice([0, 1, 2, 63, 64, 65, 127, 128, 129, rng.randint(0, 3000)]) for _ in range(bs)]
+        starts, tiles, last = welm.build_segment_tile_starts(lens)
+        assert starts.tolist() == rope_oracle.build_tile_starts(lens)
+        assert tiles == sum((x + 63) // 64 for x in lens) == welm.count_segment_tiles(lens)
+        if bs and sum(lens):
+            assert last.tolist() == list(np.cumsum(lens) - 1)
+
+
+def test_host_builder_errors():
+    lib = _native.load()
+    lens = np.array([5, -1], dtype=np.int64)
+    with pytest.raises(welm.WelmRopeError):
+        welm.count_segment_tiles(lens)
+    good = np.array([65, 1], dtype=np.int64)
+    out = np.zeros(3, dtype=np.int32)
+    tiles = ctypes.c_int64(0)
+    rc = lib.welm_rope_build_tiles_host(good.ctypes.data, 2, out.ctypes.data, 3, ctypes.byref(tiles), None)
+    assert rc == _native.ERR_CAPACITY  # needs T + 1 = 4 slots
+    out = np.zeros(4, dtype=np.int32)
+    rc = lib.welm_rope_build_tiles_host(good.ctypes.data, 2, out.ctypes.data, 4, ctypes.byref(tiles), None)
+    assert rc == _native.OK and out.tolist() == [0, 64, 65, 66] and tiles.value == 3
+    empty = welm.build_segment_tile_starts([])
+    assert empty[0].tolist() == [0] and empty[1] == 0 and empty[2].numel() == 0

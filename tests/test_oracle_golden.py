@@ -1,0 +1,97 @@
+"""Pin the oracle (and the seeded input generators) against the reference.
+
+The fixtures in tests/golden were produced by the reference's own
+``make_cos_sin_cache`` / ``make_inputs`` / ``reference_outputs``
+(bench_welmv4_inplace_rope_npu.py:1391-1521) by tests/golden/gen_golden.py.
+Here the restated oracle must reproduce every output digest bit for bit,
+and ``testfiles_b200.workloads`` must reproduce every input digest.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from conftest import digest
+from oracle import rope_oracle
+from testfiles_b200 import workloads
+
+CASES = {c.name: c for c in workloads.reference_cases() + workloads.baseline_cases()}
+
+
+def test_catalogue_matches_fixtures(golden_outputs):
+    ref_names = {n for n, r in golden_outputs.items() if r["flavour"] == "reference"}
+    assert len(ref_names) == 193
+    assert {c.name for c in workloads.reference_cases()} == ref_names
+    assert set(golden_outputs) == set(CASES)
+    for name, rec in golden_outputs.items():
+        case = CASES[name]
+        assert (case.phase, case.n_tokens, case.batch_size) == (rec["phase"], rec["n_tokens"], rec["batch_size"])
+
+
+def test_cache_restatement_matches_reference(golden_outputs):
+    ref_digest = golden_outputs["prefill_m128"]["cache"]
+    assert digest(rope_oracle.make_cos_sin_cache(32768, 100000.0)) == ref_digest
+    assert digest(workloads.make_cos_sin_cache(32768, 100000.0)) == ref_digest
+    base_digest = golden_outputs["b_prefill_m8192"]["cache"]
+    assert digest(rope_oracle.make_cos_sin_cache(16384, 10000.0)) == base_digest
+
+
+@pytest.mark.parametrize("name", sorted(CASES))
+def test_oracle_reproduces_reference(name, golden_outputs):
+    rec = golden_outputs[name]
+    case = CASES[name]
+    inp = workloads.make_inputs(case, "cpu")
+    got_inputs = {
+        "query": digest(inp.query), "key": digest(inp.key), "positions": digest(inp.positions),
+        "last_index": digest(inp.last_index), "segment_tile_starts": digest(inp.segment_tile_starts),
+    }
+    assert got_inputs == rec["inputs"], "seeded inputs differ from the reference's generators"
+    if digest(inp.cache) != rec["cache"]:
+        pytest.skip("this host's cos/sin differ in the last bit from the fixture host's")
+    q_out, k_out = rope_oracle.reference_outputs(inp.query, inp.key, inp.positions, inp.last_index, inp.cache)
+    assert digest(q_out) == rec["outputs"]["query"]
+    assert digest(k_out) == rec["outputs"]["key"]
+
+
+def test_oracle_tile_builder_matches_reference_tables(tile_tables):
+    assert len(tile_tables) == 13
+    for name, rec in tile_tables.items():
+        lens = rec["segment_lens"]
+        assert rope_oracle.build_tile_starts(lens) == rec["segment_tile_starts"], name
+        if rec["last_index"] is not None:
+            assert rope_oracle.make_last_index(sum(lens), len(lens), lens) == rec["last_index"], name
+        assert workloads.tile_starts_for(tuple(lens)) == rec["segment_tile_starts"], name
+
+
+def test_oracle_uneven_lengths():
+    assert rope_oracle.make_uneven_segment_lens(16384, 128) == workloads.reference_uneven_lens(16384, 128)
+    lens = workloads.seeded_uneven_lens(9616, 128, 5)
+    assert sum(lens) == 9616 and min(lens) >= 1 and len(lens) == 128
+
+
+def test_oracle_legacy_last_index():
+    assert rope_oracle.make_last_index(8192, 4) == [2047, 4095, 6143, 8191]
+    assert rope_oracle.make_last_index(3, 8) == [0, 0, 0, 0, 0, 1, 1, 2]
+
+
+def test_tiled_oracle_equals_full_oracle_for_wellformed_tables():
+    case = workloads.find_case("segmented_m4096_b8_aligned")
+    inp = workloads.make_inputs(case, "cpu")
+    full = rope_oracle.reference_outputs(inp.query, inp.key, inp.positions, None, inp.cache)
+    tiled = rope_oracle.tiled_outputs(inp.query, inp.key, inp.positions, inp.cache, inp.num_work_tiles, 1,
+                                      inp.segment_tile_starts.tolist())
+    assert torch.equal(full[0], tiled[0]) and torch.equal(full[1], tiled[1])
+
+
+def test_rotated_tokens_caps_tiles_at_64():
+    # a 100-token tile rotates only its first 64 tokens (reference masking rule)
+    assert rope_oracle.rotated_tokens(120, 2, 1, [0, 100, 120]) == list(range(64)) + list(range(100, 120))
+    assert rope_oracle.rotated_tokens(130, 2, 0) == list(range(128))
+
+
+def test_position_zero_is_identity():
+    cache = rope_oracle.make_cos_sin_cache(8, 10000.0)
+    x = torch.randn(5, 6, 256, dtype=torch.bfloat16)
+    out = rope_oracle.apply_reference(x, torch.zeros(5, dtype=torch.int64), cache)
+    assert torch.equal(out, x)
