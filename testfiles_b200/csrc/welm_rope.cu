@@ -29,6 +29,8 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <cstdlib>
+#include <utility>
 
 #include "welm_rope.h"
 
@@ -69,8 +71,20 @@ struct CosSin {
   float s[kLanes];
 };
 
-__device__ __forceinline__ void raise_status(int32_t* status, int bit) {
+// Cold path, kept out of line so the hot loop's register allocation and load
+// scheduling do not depend on it.
+__device__ __noinline__ void raise_status(int32_t* status, int bit) {
   if (status != nullptr) atomicOr(status, bit);
+}
+
+// Programmatic dependent launch: wait until every grid this launch depends on
+// has completed and its memory is visible (a no-op when the launch carries no
+// programmatic dependency), then let the next grid in the stream begin its own
+// launch while this one runs.  Every kernel calls this before its first global
+// memory access, so ordering with any producer is preserved.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -213,6 +227,7 @@ __device__ __forceinline__ void rotate_row(uint16_t* __restrict__ row, int64_t p
 // the cache row is loaded once for all seven heads.
 template <bool kVec, bool kSegmented>
 __global__ void __launch_bounds__(kBlock) rope_ordinary_kernel(const RopeArgs a) {
+  pdl_enter();
   const int stride = gridDim.x * blockDim.x;
   for (int item = blockIdx.x * blockDim.x + threadIdx.x; item < a.k_items; item += stride) {
     const int part = item & (kParts - 1);
@@ -253,6 +268,7 @@ __global__ void __launch_bounds__(kBlock) rope_ordinary_kernel(const RopeArgs a)
 // tensors, so the two phases need no ordering.
 template <bool kVec, bool kSegmented>
 __global__ void __launch_bounds__(kBlock) rope_mirror_kernel(const RopeArgs a) {
+  pdl_enter();
   const int stride = gridDim.x * blockDim.x;
   const int total = a.q_items + a.k_items;
   for (int item = blockIdx.x * blockDim.x + threadIdx.x; item < total; item += stride) {
@@ -318,6 +334,7 @@ build_tiles_kernel(const int64_t* __restrict__ lens, int32_t bs, int32_t* __rest
   __shared__ int64_t s_tok[kBuildThreads];   // inclusive token scan of the chunk
   __shared__ int64_t s_tile[kBuildThreads];  // inclusive tile scan of the chunk
   __shared__ int64_t wx[kBuildWarps], wy[kBuildWarps];
+  pdl_enter();
   int64_t carry_tok = 0, carry_tile = 0;     // identical in every thread
   for (int base = 0; base < bs; base += kBuildThreads) {
     const int r = base + threadIdx.x;
@@ -399,19 +416,48 @@ unsigned grid_for(int64_t items) {
   return unsigned(need < cap ? need : cap);
 }
 
-int launch_status() {
-  return cudaGetLastError() == cudaSuccess ? WELM_ROPE_OK : WELM_ROPE_ERR_CUDA;
+// Launches carry the programmatic-stream-serialization attribute (PDL) unless
+// the environment sets WELM_ROPE_PDL=0: the grid may be scheduled while the
+// previous kernel in the stream drains, and waits in pdl_enter() before it
+// touches memory.
+bool pdl_enabled() {
+  static const bool enabled = [] {
+    const char* v = std::getenv("WELM_ROPE_PDL");
+    return !(v != nullptr && v[0] == '0');
+  }();
+  return enabled;
+}
+
+template <typename... Params, typename... Args>
+int launch(void (*kernel)(Params...), unsigned grid, unsigned block, cudaStream_t stream,
+           Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (err != cudaSuccess) {
+    cudaGetLastError();  // clear the launch error so later calls start clean
+    return WELM_ROPE_ERR_CUDA;
+  }
+  return WELM_ROPE_OK;
 }
 
 template <bool kVec, bool kSegmented>
-void launch_ordinary(const RopeArgs& a, cudaStream_t stream) {
-  rope_ordinary_kernel<kVec, kSegmented><<<grid_for(a.k_items), kBlock, 0, stream>>>(a);
+int launch_ordinary(const RopeArgs& a, cudaStream_t stream) {
+  return launch(rope_ordinary_kernel<kVec, kSegmented>, grid_for(a.k_items), kBlock, stream, a);
 }
 
 template <bool kVec, bool kSegmented>
-void launch_mirror(const RopeArgs& a, cudaStream_t stream) {
-  rope_mirror_kernel<kVec, kSegmented>
-      <<<grid_for(int64_t(a.q_items) + a.k_items), kBlock, 0, stream>>>(a);
+int launch_mirror(const RopeArgs& a, cudaStream_t stream) {
+  return launch(rope_mirror_kernel<kVec, kSegmented>, grid_for(int64_t(a.q_items) + a.k_items),
+                kBlock, stream, a);
 }
 
 // Token-phase slot count shared by both ops (the reference's tile loops).
@@ -470,12 +516,8 @@ int welm_rope_ordinary(void* q, void* k, const int64_t* positions, const float* 
   const bool vec = aligned16(q) && aligned16(k) && aligned16(cos_sin_cache) &&
                    (n_tokens <= 1 || (q_token_stride % 8 == 0 && k_token_stride % 8 == 0));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (vec) {
-    if (has_segments) launch_ordinary<true, true>(a, s); else launch_ordinary<true, false>(a, s);
-  } else {
-    if (has_segments) launch_ordinary<false, true>(a, s); else launch_ordinary<false, false>(a, s);
-  }
-  return launch_status();
+  if (vec) return has_segments ? launch_ordinary<true, true>(a, s) : launch_ordinary<true, false>(a, s);
+  return has_segments ? launch_ordinary<false, true>(a, s) : launch_ordinary<false, false>(a, s);
 }
 
 int welm_rope_mirror(void* q, void* k, const int64_t* positions, const float* cos_sin_cache,
@@ -515,12 +557,8 @@ int welm_rope_mirror(void* q, void* k, const int64_t* positions, const float* co
                    (rows <= 1 || q_token_stride % 8 == 0) &&
                    (n_tokens <= 1 || k_token_stride % 8 == 0);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (vec) {
-    if (has_segments) launch_mirror<true, true>(a, s); else launch_mirror<true, false>(a, s);
-  } else {
-    if (has_segments) launch_mirror<false, true>(a, s); else launch_mirror<false, false>(a, s);
-  }
-  return launch_status();
+  if (vec) return has_segments ? launch_mirror<true, true>(a, s) : launch_mirror<true, false>(a, s);
+  return has_segments ? launch_mirror<false, true>(a, s) : launch_mirror<false, false>(a, s);
 }
 
 int welm_rope_build_tiles(const int64_t* seq_lens, int64_t batch_size, int32_t* tile_starts,
@@ -530,10 +568,9 @@ int welm_rope_build_tiles(const int64_t* seq_lens, int64_t batch_size, int32_t* 
   if (capacity < 1) return WELM_ROPE_ERR_CAPACITY;  // starts[T] always needs a slot
   if (!tile_starts || !num_tiles_out || (batch_size > 0 && !seq_lens))
     return WELM_ROPE_ERR_NULL_POINTER;
-  build_tiles_kernel<<<1, kBuildThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      seq_lens, int32_t(batch_size), tile_starts, capacity, num_tiles_out, last_index_out,
-      device_status);
-  return launch_status();
+  return launch(build_tiles_kernel, 1, kBuildThreads, static_cast<cudaStream_t>(stream), seq_lens,
+                int32_t(batch_size), tile_starts, capacity, num_tiles_out, last_index_out,
+                device_status);
 }
 
 int welm_rope_count_tiles_host(const int64_t* seq_lens, int64_t batch_size,

@@ -1,0 +1,199 @@
+"""Launch / time any catalogue case of the in-place RoPE (profiling launcher).
+
+    python -m testfiles_b200.launcher --cases b_mirror_segmented_n16384_bs128_uneven --iters 20
+    python -m testfiles_b200.launcher --cases baseline --time --json gpurun_out/times.jsonl
+
+``--iters N`` launches the op N times eagerly on one buffer set with a fixed
+kernel name per path (``rope_ordinary_kernel`` / ``rope_mirror_kernel``), for
+``ncu -k regex:…`` captures — the B200 analogue of the reference's msprof
+launch stub (run_welmv4_inplace_rope_prod_m16384_npu.py:1-60).
+
+``--time`` measures each case the way ``bench.py`` measures its headline:
+launches replayed from a CUDA graph over rotating buffer sets (enough sets
+that more than 2 x 126 MB of algorithmic bytes are touched between reuses,
+capped at 64 sets; smaller cases therefore run partly from L2, which the
+record states), CUDA events on the launching stream, median of 5 trials.
+Each record is one JSON line whose fields follow the reference's CSV record
+(bench_welmv4_inplace_rope_npu.py:1143-1162,1529-1540): ``record_type``,
+case fields, then µs per launch, tokens/s, GB/s of algorithmic bytes and the
+fraction of the HBM peak.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import platform
+import statistics
+import sys
+from typing import Iterable, Optional
+
+import torch
+
+from . import ops, workloads
+
+L2_BYTES = 126 * 1024 * 1024
+SPEC_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+
+
+def measured_hbm_peak() -> tuple[float, str]:
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            return float(json.load(fh)["hbm_gbs"]), "measured"
+    except Exception:  # noqa: BLE001
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def case_fields(case: workloads.Case) -> dict:
+    return {
+        "case": case.name,
+        "phase": case.phase,
+        "flavour": case.flavour,
+        "path": "kv_mirror" if case.is_mirror else "normal",
+        "n_tokens": case.n_tokens,
+        "q_rows": case.q_rows,
+        "batch_size": case.batch_size,
+        "request_count": len(case.segment_lens),
+        "has_segments": int(case.is_segmented),
+        "segment_lens": "|".join(str(x) for x in case.segment_lens) if len(case.segment_lens) <= 16 else
+        f"{len(case.segment_lens)} requests",
+    }
+
+
+def select_cases(spec: str) -> list[workloads.Case]:
+    ref = workloads.reference_cases()
+    base = workloads.baseline_cases()
+    groups = {
+        "reference": ref,
+        "baseline": base,
+        "decode": [c for c in base if c.phase == "decode"],
+        "prefill": [c for c in base if c.phase == "prefill"],
+        "mirror": [c for c in base if c.is_mirror],
+        "segmented": [c for c in ref if c.phase == "segmented_prefill"],
+    }
+    out: list[workloads.Case] = []
+    for item in spec.split(","):
+        item = item.strip()
+        if not item:
+            continue
+        out.extend(groups[item] if item in groups else [workloads.find_case(item)])
+    return out
+
+
+def _launch(inp: workloads.Inputs) -> None:
+    ops.welmv4_inplace_rope_npu(inp.query, inp.key, inp.positions, inp.cache, inp.last_index,
+                                inp.segment_tile_starts)
+
+
+def time_case(case: workloads.Case, device: torch.device, trials: int = 5, graph_launches: int = 64,
+              replays: Optional[int] = None) -> dict:
+    """µs per launch of ``case`` (graph-replayed over rotating buffer sets)."""
+    host = workloads.make_inputs(case, "cpu")
+    nbytes = workloads.min_bytes(case)
+    sets_needed = max(2, -(-2 * L2_BYTES // max(nbytes, 1)))
+    sets = int(min(64, sets_needed))
+    buffers = []
+    base = host.to(device)
+    for _ in range(sets):
+        b = base.clone()
+        b.positions = base.positions.clone()
+        b.cache = base.cache.clone()
+        buffers.append(b)
+    for i in range(3):
+        _launch(buffers[i % sets])
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(graph_launches):
+            _launch(buffers[i % sets])
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize(device)
+    if replays is None:  # about 5 ms of launches per trial
+        est_us = 1.5 + nbytes / 5e6
+        replays = max(5, min(200, int(5e3 / (est_us * graph_launches))))
+    stream = torch.cuda.current_stream(device)
+    samples = []
+    for _ in range(trials):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(replays):
+            graph.replay()
+        end.record(stream)
+        end.synchronize()
+        samples.append(start.elapsed_time(end) * 1e3 / (replays * graph_launches))
+    del graph
+    us = statistics.median(samples)
+    peak, kind = measured_hbm_peak()
+    gbs = nbytes / (us * 1e3)
+    return {
+        "record_type": "timing",
+        **case_fields(case),
+        "us_per_launch": round(us, 3),
+        "tokens_per_s": round(case.n_tokens / (us * 1e-6), 1),
+        "bytes_per_launch": nbytes,
+        "gb_s": round(gbs, 1),
+        "hbm_frac": round(gbs / peak, 4),
+        "hbm_peak_gbs": peak,
+        "hbm_peak_source": kind,
+        "hbm_frac_of_8tbs_spec": round(gbs / SPEC_HBM_GBS, 4),
+        "buffer_sets": sets,
+        "l2_cold": bool(sets * nbytes > 2 * L2_BYTES),
+        "pdl": os.environ.get("WELM_ROPE_PDL", "1") != "0",
+        "device_name": torch.cuda.get_device_name(device),
+        "torch_version": torch.__version__,
+        "python_version": platform.python_version(),
+    }
+
+
+def launch_case(case: workloads.Case, device: torch.device, iters: int) -> dict:
+    inp = workloads.make_inputs(case, device)
+    for _ in range(iters):
+        _launch(inp)
+    torch.cuda.synchronize(device)
+    return {"record_type": "launch", **case_fields(case), "iters": iters,
+            "kernel_name": "rope_mirror_kernel" if case.is_mirror else "rope_ordinary_kernel"}
+
+
+def run(cases: Iterable[workloads.Case], device: torch.device, time_it: bool, iters: int,
+        out: Optional[str]) -> list[dict]:
+    records = []
+    sink = open(out, "a") if out else None
+    try:
+        for case in cases:
+            rec = time_case(case, device) if time_it else launch_case(case, device, iters)
+            records.append(rec)
+            line = json.dumps(rec)
+            print(line, flush=True)
+            if sink:
+                sink.write(line + "\n")
+                sink.flush()
+    finally:
+        if sink:
+            sink.close()
+    return records
+
+
+def main(argv: Optional[list[str]] = None) -> int:
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("--cases", default="b_prefill_m16384",
+                        help="case names or groups (reference, baseline, decode, prefill, mirror, segmented)")
+    parser.add_argument("--time", action="store_true", help="time each case (graph replay, rotating buffers)")
+    parser.add_argument("--iters", type=int, default=20, help="eager launches per case (without --time)")
+    parser.add_argument("--device", default="cuda:0")
+    parser.add_argument("--json", default=None, help="append JSON lines here")
+    args = parser.parse_args(argv)
+    if not torch.cuda.is_available():
+        print("the launcher needs a CUDA device", file=sys.stderr)
+        return 2
+    device = torch.device(args.device)
+    torch.cuda.set_device(device)
+    run(select_cases(args.cases), device, args.time, args.iters, args.json)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

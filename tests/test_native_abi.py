@@ -144,3 +144,16 @@ def test_host_builder_errors():
     assert rc == _native.OK and out.tolist() == [0, 64, 65, 66] and tiles.value == 3
     empty = welm.build_segment_tile_starts([])
     assert empty[0].tolist() == [0] and empty[1] == 0 and empty[2].numel() == 0
+
+
+def test_launcher_case_selection_and_fields():
+    from testfiles_b200 import launcher, workloads
+
+    assert len(launcher.select_cases("decode")) == 128
+    assert len(launcher.select_cases("reference")) == 193
+    cases = launcher.select_cases("b_prefill_m16384,mirror_segmented_m16384_b128_uneven")
+    assert [c.name for c in cases] == ["b_prefill_m16384", "mirror_segmented_m16384_b128_uneven"]
+    fields = launcher.case_fields(cases[1])
+    assert fields["path"] == "kv_mirror" and fields["has_segments"] == 1 and fields["batch_size"] == 128
+    assert workloads.min_bytes(cases[0]) == 2056 * 16384
+    assert workloads.min_bytes(cases[1]) == 520 * 16384 + 1544 * 128 + 4 * 321
