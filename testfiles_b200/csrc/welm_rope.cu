@@ -64,6 +64,7 @@ struct RopeArgs {
   int32_t* status;             // optional device status word
   int32_t q_items;             // Q-row items (mirror): BS * kParts
   int32_t k_items;             // token items: tokens (or tile slots) * kParts
+  int32_t num_tiles;           // work tiles (segmented)
 };
 
 struct CosSin {
@@ -171,123 +172,275 @@ __device__ __forceinline__ void rotate8(uint4& x1, uint4& x2, const CosSin& cs) 
 }
 
 // ---------------------------------------------------------------------------
-// Token resolution for the token-phase slot `slot` (one slot per token of a
-// dense range, or 64 slots per work tile when segmented).  Returns false when
-// the slot is empty (tile tail) or out of range (then a status bit is raised).
-// Tile semantics are the reference kernels' (bench_welmv4_inplace_rope_npu.py:
-// 700-718, 856-867): tile i covers [starts[i], starts[i] + min(64, len)).
+// Row pieces.  Slices<NH> holds NH heads (head stride 256 lanes) of one row for
+// one part; its loads are issued by load() and consumed by rotate_store(), so
+// callers can put the position / cache gather and the tile check in between.
 // ---------------------------------------------------------------------------
-template <bool kSegmented>
-__device__ __forceinline__ bool resolve_token(const RopeArgs& a, int slot, int part, int64_t& tok) {
-  if (!kSegmented) {
-    tok = slot;  // the host sized k_items to min(N, 64 * num_work_tiles)
+template <bool kVec, int NH>
+struct Slices {
+  uint16_t* base;
+  uint4 x1[NH], x2[NH];
+  __device__ __forceinline__ void load(uint16_t* row, int part) {
+    base = row + kRopeLane0 + part * kLanes;
+#pragma unroll
+    for (int h = 0; h < NH; ++h) {
+      x1[h] = Io<kVec>::load8(base + h * kHeadDim);
+      x2[h] = Io<kVec>::load8(base + h * kHeadDim + kHalf);
+    }
+  }
+  __device__ __forceinline__ void rotate_store(const CosSin& cs) {
+#pragma unroll
+    for (int h = 0; h < NH; ++h) {
+      rotate8(x1[h], x2[h], cs);
+      Io<kVec>::store8(base + h * kHeadDim, x1[h]);
+      Io<kVec>::store8(base + h * kHeadDim + kHalf, x2[h]);
+    }
+  }
+};
+
+// Gathers this part's cos/sin at `pos`; false when pos is outside the cache
+// (nothing is read then).
+template <bool kVec>
+__device__ __forceinline__ bool gather_cos_sin(const RopeArgs& a, int64_t pos, int part, CosSin& cs) {
+  if (pos < 0 || pos >= a.max_position) return false;
+  Io<kVec>::load_cos_sin(a.cache + pos * kRopeDim, part, cs);
+  return true;
+}
+
+// ---------------------------------------------------------------------------
+// Token sources.  Tile semantics are the reference kernels'
+// (bench_welmv4_inplace_rope_npu.py:700-718, 856-867): tile i covers
+// [starts[i], starts[i] + min(64, starts[i+1] - starts[i])).
+//   kDense:     has_segments = 0; token = slot, slots = min(N, 64 * tiles).
+//   kTileTable: has_segments = 1 with a table that fits in shared memory;
+//               items are tokens 0..N-1 in order, so every load is issued at
+//               once, and a token is rotated iff a tile covers it (binary
+//               search of the staged table, done while the loads fly).
+//               Exact for any non-decreasing table; other tables are flagged.
+//   kTileSlots: has_segments = 1 with a large table; 64 slots per tile,
+//               token = starts[tile] + slot (one extra dependent load).
+// ---------------------------------------------------------------------------
+enum class Source { kDense, kTileTable, kTileSlots };
+
+constexpr int kTableCap = 2048;  // staged table entries (8 KB of shared memory)
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// Starts copying tile_starts[0..n) into shared memory (4-byte cp.async; the
+// table is only 4-byte aligned).
+__device__ __forceinline__ void stage_table_async(int32_t* s_tab, const int32_t* g_tab, int n) {
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(s_tab + j)), "l"(g_tab + j)
+                 : "memory");
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+__device__ __forceinline__ void stage_table_wait() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
+}
+
+// Whether a non-decreasing tile table rotates token t: the last tile starting
+// at or before t must hold t within its first 64 tokens.
+__device__ __forceinline__ bool table_covers(const int32_t* s_tab, int num_tiles, int64_t t) {
+  int lo = 0, hi = num_tiles + 1;  // first entry greater than t
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (s_tab[mid] <= t) lo = mid + 1; else hi = mid;
+  }
+  const int i = lo - 1;
+  return i >= 0 && i < num_tiles && t - s_tab[i] < kTile;
+}
+
+// Tile validation item: flags a tile that starts below 0, ends past N, runs
+// backwards or holds more than 64 tokens.
+__device__ __forceinline__ void check_tile(const RopeArgs& a, int tile) {
+  const int64_t begin = __ldg(a.tile_starts + tile);
+  const int64_t end = __ldg(a.tile_starts + tile + 1);
+  if (begin < 0 || end < begin || end - begin > kTile || end > a.n_tokens)
+    raise_status(a.status, WELM_ROPE_DEV_BAD_TILE);
+}
+
+// Slot -> token for kDense and kTileSlots.  False when the slot is empty (a
+// short tile's tail) or its token is outside [0, N) (never touched).
+template <Source kSrc>
+__device__ __forceinline__ bool slot_token(const RopeArgs& a, int slot, int part, int64_t& tok) {
+  if (kSrc == Source::kDense) {
+    tok = slot;
     return true;
   }
   const int tile = slot / kTile;
   const int j = slot - tile * kTile;
   const int64_t begin = __ldg(a.tile_starts + tile);
   const int64_t end = __ldg(a.tile_starts + tile + 1);
-  int64_t count = end - begin;
-  if (j == 0 && part == 0 && (begin < 0 || end > a.n_tokens || count < 0 || count > kTile))
+  if (j == 0 && part == 0 && (begin < 0 || end < begin || end - begin > kTile || end > a.n_tokens))
     raise_status(a.status, WELM_ROPE_DEV_BAD_TILE);
-  if (count > kTile) count = kTile;
+  const int64_t count = end - begin < kTile ? end - begin : kTile;
   if (j >= count) return false;
   tok = begin + j;
-  return tok >= 0 && tok < a.n_tokens;  // out-of-range tokens are skipped, never touched
+  return tok >= 0 && tok < a.n_tokens;
 }
 
-// Rotates NH heads (head stride 256 lanes) of one row for one part.  All data
-// loads are issued before the position check and the cache gather.
-template <bool kVec, int NH>
-__device__ __forceinline__ void rotate_row(uint16_t* __restrict__ row, int64_t pos,
-                                           const RopeArgs& a, int part, int bad_bit) {
-  uint16_t* base = row + kRopeLane0 + part * kLanes;
-  uint4 x1[NH], x2[NH];
-#pragma unroll
-  for (int h = 0; h < NH; ++h) {
-    x1[h] = Io<kVec>::load8(base + h * kHeadDim);
-    x2[h] = Io<kVec>::load8(base + h * kHeadDim + kHalf);
+// ---------------------------------------------------------------------------
+// Ordinary prefill / decode: K head + 6 Q heads of token t at positions[t];
+// the cache row is gathered once for all seven heads.
+// ---------------------------------------------------------------------------
+template <bool kVec>
+__device__ __forceinline__ void ordinary_token(const RopeArgs& a, int64_t tok, int part) {
+  const int64_t pos = __ldg(a.positions + tok);
+  Slices<kVec, 1> kx;
+  Slices<kVec, kQHeads> qx;
+  kx.load(a.k + tok * a.k_stride, part);
+  qx.load(a.q + tok * a.q_stride, part);
+  CosSin cs;
+  if (!gather_cos_sin<kVec>(a, pos, part, cs)) {
+    if (part == 0) raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
+    return;
   }
-  if (pos < 0 || pos >= a.max_position) {
-    if (part == 0) raise_status(a.status, bad_bit);
+  kx.rotate_store(cs);
+  qx.rotate_store(cs);
+}
+
+template <bool kVec, Source kSrc>
+__global__ void __launch_bounds__(kBlock) rope_ordinary_kernel(const RopeArgs a) {
+  extern __shared__ int32_t s_tab[];
+  pdl_enter();
+  if constexpr (kSrc == Source::kTileTable) {
+    // One item per thread: tokens [0, k_items / 4), then one check per tile.
+    stage_table_async(s_tab, a.tile_starts, a.num_tiles + 1);
+    const int item = blockIdx.x * blockDim.x + threadIdx.x;
+    const int part = item & (kParts - 1);
+    const bool is_token = item < a.k_items;
+    const int64_t tok = is_token ? (item >> kPartShift) : 0;
+    Slices<kVec, 1> kx;
+    Slices<kVec, kQHeads> qx;
+    CosSin cs;
+    bool pos_ok = false;
+    if (is_token) {
+      const int64_t pos = __ldg(a.positions + tok);
+      kx.load(a.k + tok * a.k_stride, part);
+      qx.load(a.q + tok * a.q_stride, part);
+      pos_ok = gather_cos_sin<kVec>(a, pos, part, cs);
+    } else if (item - a.k_items < a.num_tiles) {
+      check_tile(a, item - a.k_items);
+    }
+    stage_table_wait();  // every thread of the CTA reaches this once
+    if (is_token && table_covers(s_tab, a.num_tiles, tok)) {
+      if (pos_ok) {
+        kx.rotate_store(cs);
+        qx.rotate_store(cs);
+      } else if (part == 0) {
+        raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
+      }
+    }
+  } else {
+    const int stride = gridDim.x * blockDim.x;
+    for (int item = blockIdx.x * blockDim.x + threadIdx.x; item < a.k_items; item += stride) {
+      const int part = item & (kParts - 1);
+      int64_t tok;
+      if (slot_token<kSrc>(a, item >> kPartShift, part, tok)) ordinary_token<kVec>(a, tok, part);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// KV-mirror prefill.  Items [0, q_items) are the BS Q rows (6 heads at
+// positions[last_index[b]], bench_welmv4_inplace_rope_npu.py:839-854); the
+// next k_items are K tokens (1 head at positions[t],
+// bench_welmv4_inplace_rope_npu.py:856-919).  Q rows and K rows are disjoint
+// tensors, so the two phases need no ordering.  A Q row's data loads are
+// issued before its last_index -> position -> cache chain.
+// ---------------------------------------------------------------------------
+template <bool kVec>
+__device__ __forceinline__ void finish_q_row(const RopeArgs& a, Slices<kVec, kQHeads>& qx, int64_t src,
+                                             int part) {
+  if (src < 0 || src >= a.n_tokens) {
+    if (part == 0) raise_status(a.status, WELM_ROPE_DEV_BAD_LAST_INDEX);
     return;
   }
   CosSin cs;
-  Io<kVec>::load_cos_sin(a.cache + pos * kRopeDim, part, cs);
-#pragma unroll
-  for (int h = 0; h < NH; ++h) {
-    rotate8(x1[h], x2[h], cs);
-    Io<kVec>::store8(base + h * kHeadDim, x1[h]);
-    Io<kVec>::store8(base + h * kHeadDim + kHalf, x2[h]);
+  if (!gather_cos_sin<kVec>(a, __ldg(a.positions + src), part, cs)) {
+    if (part == 0) raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
+    return;
   }
+  qx.rotate_store(cs);
 }
 
-// Ordinary prefill / decode: K head + 6 Q heads of token t at positions[t].
-// K and Q are fused into one 7-head row pass when both are 16-byte capable;
-// the cache row is loaded once for all seven heads.
-template <bool kVec, bool kSegmented>
-__global__ void __launch_bounds__(kBlock) rope_ordinary_kernel(const RopeArgs a) {
-  pdl_enter();
-  const int stride = gridDim.x * blockDim.x;
-  for (int item = blockIdx.x * blockDim.x + threadIdx.x; item < a.k_items; item += stride) {
-    const int part = item & (kParts - 1);
-    int64_t tok;
-    if (!resolve_token<kSegmented>(a, item >> kPartShift, part, tok)) continue;
-    const int64_t pos = __ldg(a.positions + tok);
-    uint16_t* kbase = a.k + tok * a.k_stride + kRopeLane0 + part * kLanes;
-    uint16_t* qbase = a.q + tok * a.q_stride + kRopeLane0 + part * kLanes;
-    uint4 kx1 = Io<kVec>::load8(kbase), kx2 = Io<kVec>::load8(kbase + kHalf);
-    uint4 qx1[kQHeads], qx2[kQHeads];
-#pragma unroll
-    for (int h = 0; h < kQHeads; ++h) {
-      qx1[h] = Io<kVec>::load8(qbase + h * kHeadDim);
-      qx2[h] = Io<kVec>::load8(qbase + h * kHeadDim + kHalf);
-    }
-    if (pos < 0 || pos >= a.max_position) {
-      if (part == 0) raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
-      continue;
-    }
-    CosSin cs;
-    Io<kVec>::load_cos_sin(a.cache + pos * kRopeDim, part, cs);
-    rotate8(kx1, kx2, cs);
-    Io<kVec>::store8(kbase, kx1);
-    Io<kVec>::store8(kbase + kHalf, kx2);
-#pragma unroll
-    for (int h = 0; h < kQHeads; ++h) {
-      rotate8(qx1[h], qx2[h], cs);
-      Io<kVec>::store8(qbase + h * kHeadDim, qx1[h]);
-      Io<kVec>::store8(qbase + h * kHeadDim + kHalf, qx2[h]);
-    }
-  }
+template <bool kVec>
+__device__ __forceinline__ void mirror_q_row(const RopeArgs& a, int b, int part) {
+  Slices<kVec, kQHeads> qx;
+  qx.load(a.q + int64_t(b) * a.q_stride, part);
+  finish_q_row<kVec>(a, qx, __ldg(a.last_index + b), part);
 }
 
-// KV-mirror prefill.  Items [0, q_items) are the BS Q rows (6 heads at
-// positions[last_index[b]], bench_welmv4_inplace_rope_npu.py:839-854); items
-// [q_items, q_items + k_items) are the K tokens (1 head at positions[t],
-// bench_welmv4_inplace_rope_npu.py:856-919).  Q rows and K rows are disjoint
-// tensors, so the two phases need no ordering.
-template <bool kVec, bool kSegmented>
+template <bool kVec>
+__device__ __forceinline__ void mirror_k_token(const RopeArgs& a, int64_t tok, int part) {
+  const int64_t pos = __ldg(a.positions + tok);
+  Slices<kVec, 1> kx;
+  kx.load(a.k + tok * a.k_stride, part);
+  CosSin cs;
+  if (!gather_cos_sin<kVec>(a, pos, part, cs)) {
+    if (part == 0) raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
+    return;
+  }
+  kx.rotate_store(cs);
+}
+
+template <bool kVec, Source kSrc>
 __global__ void __launch_bounds__(kBlock) rope_mirror_kernel(const RopeArgs a) {
+  extern __shared__ int32_t s_tab[];
   pdl_enter();
-  const int stride = gridDim.x * blockDim.x;
-  const int total = a.q_items + a.k_items;
-  for (int item = blockIdx.x * blockDim.x + threadIdx.x; item < total; item += stride) {
+  if constexpr (kSrc == Source::kTileTable) {
+    // One item per thread: Q rows, then tokens [0, k_items / 4), then one
+    // check per tile.  Every thread reaches the single barrier below in
+    // uniform control flow: phase 1 issues the loads of whatever item the
+    // thread owns, phase 2 finishes it.
+    stage_table_async(s_tab, a.tile_starts, a.num_tiles + 1);
+    const int item = blockIdx.x * blockDim.x + threadIdx.x;
     const int part = item & (kParts - 1);
-    if (item < a.q_items) {
-      const int b = item >> kPartShift;
-      uint16_t* row = a.q + int64_t(b) * a.q_stride;
-      const int64_t src = __ldg(a.last_index + b);
-      if (src < 0 || src >= a.n_tokens) {
-        if (part == 0) raise_status(a.status, WELM_ROPE_DEV_BAD_LAST_INDEX);
-        continue;
+    const bool is_q = item < a.q_items;
+    const int k_item = item - a.q_items;
+    const bool is_token = !is_q && k_item < a.k_items;
+    const int64_t tok = is_token ? (k_item >> kPartShift) : 0;
+    Slices<kVec, kQHeads> qx;
+    Slices<kVec, 1> kx;
+    CosSin cs;
+    bool pos_ok = false;
+    int64_t src = 0;
+    if (is_q) {
+      qx.load(a.q + int64_t(item >> kPartShift) * a.q_stride, part);
+      src = __ldg(a.last_index + (item >> kPartShift));
+    } else if (is_token) {
+      const int64_t pos = __ldg(a.positions + tok);
+      kx.load(a.k + tok * a.k_stride, part);
+      pos_ok = gather_cos_sin<kVec>(a, pos, part, cs);
+    } else if (k_item - a.k_items < a.num_tiles) {
+      check_tile(a, k_item - a.k_items);
+    }
+    stage_table_wait();
+    if (is_q) {
+      finish_q_row<kVec>(a, qx, src, part);
+    } else if (is_token && table_covers(s_tab, a.num_tiles, tok)) {
+      if (pos_ok) {
+        kx.rotate_store(cs);
+      } else if (part == 0) {
+        raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
       }
-      rotate_row<kVec, kQHeads>(row, __ldg(a.positions + src), a, part,
-                                WELM_ROPE_DEV_BAD_POSITION);
-    } else {
-      int64_t tok;
-      if (!resolve_token<kSegmented>(a, (item - a.q_items) >> kPartShift, part, tok)) continue;
-      rotate_row<kVec, 1>(a.k + tok * a.k_stride, __ldg(a.positions + tok), a, part,
-                          WELM_ROPE_DEV_BAD_POSITION);
+    }
+  } else {
+    const int stride = gridDim.x * blockDim.x;
+    const int total = a.q_items + a.k_items;
+    for (int item = blockIdx.x * blockDim.x + threadIdx.x; item < total; item += stride) {
+      const int part = item & (kParts - 1);
+      if (item < a.q_items) {
+        mirror_q_row<kVec>(a, item >> kPartShift, part);
+      } else {
+        int64_t tok;
+        if (slot_token<kSrc>(a, (item - a.q_items) >> kPartShift, part, tok)) mirror_k_token<kVec>(a, tok, part);
+      }
     }
   }
 }
@@ -405,10 +558,9 @@ int current_sm_count() {
   return sms;
 }
 
-// Grid for `items` work items: enough CTAs for one item per thread, capped at
-// what the device keeps resident (16 CTAs of 128 threads per SM, the
-// register-limited residency of these kernels) so the grid-stride loop covers
-// larger inputs.
+// Grid for `items` work items of a grid-stride kernel: enough CTAs for one
+// item per thread, capped at 16 CTAs of 128 threads per SM (more than these
+// kernels keep resident) so larger inputs loop.
 unsigned grid_for(int64_t items) {
   const int sms = current_sm_count();
   const int64_t need = (items + kBlock - 1) / kBlock;
@@ -429,12 +581,12 @@ bool pdl_enabled() {
 }
 
 template <typename... Params, typename... Args>
-int launch(void (*kernel)(Params...), unsigned grid, unsigned block, cudaStream_t stream,
+int launch(void (*kernel)(Params...), unsigned grid, unsigned block, size_t smem, cudaStream_t stream,
            Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(block);
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -449,22 +601,49 @@ int launch(void (*kernel)(Params...), unsigned grid, unsigned block, cudaStream_
   return WELM_ROPE_OK;
 }
 
-template <bool kVec, bool kSegmented>
-int launch_ordinary(const RopeArgs& a, cudaStream_t stream) {
-  return launch(rope_ordinary_kernel<kVec, kSegmented>, grid_for(a.k_items), kBlock, stream, a);
+// How the token phase is laid out for one call (see Source).
+struct Plan {
+  Source src;
+  int64_t token_items;  // items of the token phase
+  int64_t check_items;  // tile validation items (kTileTable only)
+};
+
+Plan plan_tokens(int64_t has_segments, int64_t num_work_tiles, int64_t n_tokens) {
+  if (!has_segments) {
+    const int64_t covered = num_work_tiles * kTile;
+    return {Source::kDense, (covered < n_tokens ? covered : n_tokens) * kParts, 0};
+  }
+  if (num_work_tiles == 0 || n_tokens == 0) return {Source::kTileSlots, 0, 0};
+  if (num_work_tiles + 1 <= kTableCap) return {Source::kTileTable, n_tokens * kParts, num_work_tiles};
+  return {Source::kTileSlots, num_work_tiles * kTile * kParts, 0};
 }
 
-template <bool kVec, bool kSegmented>
-int launch_mirror(const RopeArgs& a, cudaStream_t stream) {
-  return launch(rope_mirror_kernel<kVec, kSegmented>, grid_for(int64_t(a.q_items) + a.k_items),
-                kBlock, stream, a);
+template <typename Kernel>
+int launch_plan(Kernel kernel, const Plan& plan, const RopeArgs& a, cudaStream_t stream) {
+  const int64_t total = int64_t(a.q_items) + plan.token_items + plan.check_items;
+  if (plan.src == Source::kTileTable) {
+    const size_t smem = (size_t(a.num_tiles + 1) * sizeof(int32_t) + 15) & ~size_t(15);
+    return launch(kernel, unsigned((total + kBlock - 1) / kBlock), kBlock, smem, stream, a);
+  }
+  return launch(kernel, grid_for(total), kBlock, 0, stream, a);
 }
 
-// Token-phase slot count shared by both ops (the reference's tile loops).
-int64_t token_slots(int64_t has_segments, int64_t num_work_tiles, int64_t n_tokens) {
-  if (has_segments) return num_work_tiles * kTile;
-  const int64_t covered = num_work_tiles * kTile;
-  return covered < n_tokens ? covered : n_tokens;
+template <bool kVec>
+int launch_ordinary(const Plan& plan, const RopeArgs& a, cudaStream_t s) {
+  switch (plan.src) {
+    case Source::kDense: return launch_plan(rope_ordinary_kernel<kVec, Source::kDense>, plan, a, s);
+    case Source::kTileTable: return launch_plan(rope_ordinary_kernel<kVec, Source::kTileTable>, plan, a, s);
+    default: return launch_plan(rope_ordinary_kernel<kVec, Source::kTileSlots>, plan, a, s);
+  }
+}
+
+template <bool kVec>
+int launch_mirror(const Plan& plan, const RopeArgs& a, cudaStream_t s) {
+  switch (plan.src) {
+    case Source::kDense: return launch_plan(rope_mirror_kernel<kVec, Source::kDense>, plan, a, s);
+    case Source::kTileTable: return launch_plan(rope_mirror_kernel<kVec, Source::kTileTable>, plan, a, s);
+    default: return launch_plan(rope_mirror_kernel<kVec, Source::kTileSlots>, plan, a, s);
+  }
 }
 
 }  // namespace
@@ -493,9 +672,10 @@ int welm_rope_ordinary(void* q, void* k, const int64_t* positions, const float* 
                        void* stream) {
   if (has_segments != 0 && has_segments != 1) return WELM_ROPE_ERR_BAD_MODE;
   if (num_work_tiles < 0 || n_tokens < 0 || max_position < 0) return WELM_ROPE_ERR_BAD_SIZE;
-  const int64_t slots = token_slots(has_segments, num_work_tiles, n_tokens);
-  if (slots > kMaxItems / kParts) return WELM_ROPE_ERR_BAD_SIZE;
-  if (slots == 0 || n_tokens == 0) return WELM_ROPE_OK;  // nothing to rotate
+  if (num_work_tiles > kMaxItems / (kTile * kParts) || n_tokens > kMaxItems / kParts)
+    return WELM_ROPE_ERR_BAD_SIZE;
+  const Plan plan = plan_tokens(has_segments, num_work_tiles, n_tokens);
+  if (plan.token_items == 0) return WELM_ROPE_OK;  // nothing to rotate
   if (!q || !k || !positions || !cos_sin_cache) return WELM_ROPE_ERR_NULL_POINTER;
   if (has_segments && !segment_tile_starts) return WELM_ROPE_ERR_NULL_POINTER;
   if (n_tokens > 1 && (q_token_stride < kQHeads * kHeadDim || k_token_stride < kHeadDim))
@@ -512,12 +692,12 @@ int welm_rope_ordinary(void* q, void* k, const int64_t* positions, const float* 
   a.n_tokens = n_tokens;
   a.max_position = max_position;
   a.status = device_status;
-  a.k_items = int32_t(slots * kParts);
+  a.k_items = int32_t(plan.token_items);
+  a.num_tiles = int32_t(num_work_tiles);
   const bool vec = aligned16(q) && aligned16(k) && aligned16(cos_sin_cache) &&
                    (n_tokens <= 1 || (q_token_stride % 8 == 0 && k_token_stride % 8 == 0));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (vec) return has_segments ? launch_ordinary<true, true>(a, s) : launch_ordinary<true, false>(a, s);
-  return has_segments ? launch_ordinary<false, true>(a, s) : launch_ordinary<false, false>(a, s);
+  return vec ? launch_ordinary<true>(plan, a, s) : launch_ordinary<false>(plan, a, s);
 }
 
 int welm_rope_mirror(void* q, void* k, const int64_t* positions, const float* cos_sin_cache,
@@ -528,14 +708,17 @@ int welm_rope_mirror(void* q, void* k, const int64_t* positions, const float* co
   if (has_segments != 0 && has_segments != 1) return WELM_ROPE_ERR_BAD_MODE;
   if (num_work_tiles < 0 || n_tokens < 0 || batch_size < 0 || max_position < 0)
     return WELM_ROPE_ERR_BAD_SIZE;
-  const int64_t slots = n_tokens > 0 ? token_slots(has_segments, num_work_tiles, n_tokens) : 0;
-  const int64_t rows = n_tokens > 0 ? batch_size : 0;  // Q rows need a valid last_index target
-  if (slots > kMaxItems / kParts || rows > kMaxItems / kParts ||
-      (slots + rows) * kParts > kMaxItems)
+  if (num_work_tiles > kMaxItems / (kTile * kParts) || n_tokens > kMaxItems / kParts ||
+      batch_size > kMaxItems / kParts)
     return WELM_ROPE_ERR_BAD_SIZE;
-  if (slots == 0 && rows == 0) return WELM_ROPE_OK;
-  if (!q || !k || !positions || !cos_sin_cache || !last_index) return WELM_ROPE_ERR_NULL_POINTER;
-  if (has_segments && slots > 0 && !segment_tile_starts) return WELM_ROPE_ERR_NULL_POINTER;
+  const Plan plan = n_tokens > 0 ? plan_tokens(has_segments, num_work_tiles, n_tokens) : Plan{Source::kDense, 0, 0};
+  const int64_t rows = n_tokens > 0 ? batch_size : 0;  // Q rows need a valid last_index target
+  if (rows * kParts + plan.token_items + plan.check_items > kMaxItems) return WELM_ROPE_ERR_BAD_SIZE;
+  if (plan.token_items == 0 && rows == 0) return WELM_ROPE_OK;
+  if (!positions || !cos_sin_cache) return WELM_ROPE_ERR_NULL_POINTER;
+  if (rows > 0 && (!q || !last_index)) return WELM_ROPE_ERR_NULL_POINTER;
+  if (plan.token_items > 0 && !k) return WELM_ROPE_ERR_NULL_POINTER;
+  if (has_segments && plan.token_items > 0 && !segment_tile_starts) return WELM_ROPE_ERR_NULL_POINTER;
   if ((rows > 1 && q_token_stride < kQHeads * kHeadDim) || (n_tokens > 1 && k_token_stride < kHeadDim))
     return WELM_ROPE_ERR_BAD_STRIDE;
 
@@ -552,13 +735,13 @@ int welm_rope_mirror(void* q, void* k, const int64_t* positions, const float* co
   a.max_position = max_position;
   a.status = device_status;
   a.q_items = int32_t(rows * kParts);
-  a.k_items = int32_t(slots * kParts);
+  a.k_items = int32_t(plan.token_items);
+  a.num_tiles = int32_t(num_work_tiles);
   const bool vec = aligned16(q) && aligned16(k) && aligned16(cos_sin_cache) &&
                    (rows <= 1 || q_token_stride % 8 == 0) &&
                    (n_tokens <= 1 || k_token_stride % 8 == 0);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (vec) return has_segments ? launch_mirror<true, true>(a, s) : launch_mirror<true, false>(a, s);
-  return has_segments ? launch_mirror<false, true>(a, s) : launch_mirror<false, false>(a, s);
+  return vec ? launch_mirror<true>(plan, a, s) : launch_mirror<false>(plan, a, s);
 }
 
 int welm_rope_build_tiles(const int64_t* seq_lens, int64_t batch_size, int32_t* tile_starts,
@@ -568,7 +751,7 @@ int welm_rope_build_tiles(const int64_t* seq_lens, int64_t batch_size, int32_t* 
   if (capacity < 1) return WELM_ROPE_ERR_CAPACITY;  // starts[T] always needs a slot
   if (!tile_starts || !num_tiles_out || (batch_size > 0 && !seq_lens))
     return WELM_ROPE_ERR_NULL_POINTER;
-  return launch(build_tiles_kernel, 1, kBuildThreads, static_cast<cudaStream_t>(stream), seq_lens,
+  return launch(build_tiles_kernel, 1, kBuildThreads, 0, static_cast<cudaStream_t>(stream), seq_lens,
                 int32_t(batch_size), tile_starts, capacity, num_tiles_out, last_index_out,
                 device_status);
 }

@@ -178,20 +178,22 @@ def test_mirror_bad_last_index_is_skipped_and_flagged():
     assert_bitexact(kd, rope_oracle.apply_reference(inp.key, inp.positions, inp.cache), "key")
 
 
+@pytest.mark.parametrize("pad", [0, 2100])
 @pytest.mark.parametrize("mirror", [False, True])
-def test_irregular_tile_tables_follow_reference_masking(mirror):
+def test_irregular_tile_tables_follow_reference_masking(mirror, pad):
     """Tiles longer than 64 rotate only their first 64 tokens; empty tiles and
     tiles past N rotate nothing; non-contiguous positions inside a tile use
-    each token's own position (per-token gather)."""
-    n = 400
+    each token's own position (per-token gather).  pad=2100 prepends 1-token
+    tiles so the table exceeds the shared-memory path (slot path)."""
+    n = 400 + pad
     inp = small_inputs(n, 5)
-    table = [0, 100, 100, 130, 250, 390, 400]  # 100-token tile, empty tile, 120-token tile, ...
+    table = list(range(pad)) + [pad + x for x in (0, 100, 100, 130, 250, 390, 400)]
     starts = torch.tensor(table, dtype=torch.int32)
     tiles = len(table) - 1
     status = torch.zeros(1, dtype=torch.int32, device=DEV)
     dev = inp.to(DEV)
     if mirror:
-        last = torch.tensor([99, 399], dtype=torch.int64)
+        last = torch.tensor([99 + pad, 399 + pad], dtype=torch.int64)
         q = torch.randn((2, 6, 256), dtype=torch.bfloat16)
         qd = q.to(DEV)
         welm.rope_mirror_prefill(qd, dev.key, dev.positions, dev.cache, last.to(DEV), starts.to(DEV), tiles, n,
@@ -245,6 +247,12 @@ def test_empty_inputs_are_noops():
     welm.welmv4_inplace_rope_npu(q, k, pos, cache)
     welm.welmv4_inplace_rope_npu(q, k, pos, cache, torch.empty(0, dtype=torch.int64, device=DEV))
     torch.cuda.synchronize()
+    # KV mirror with no Q rows: K is still rotated
+    inp = small_inputs(70, 15)
+    dev = inp.to(DEV)
+    welm.welmv4_inplace_rope_npu(q, dev.key, dev.positions, dev.cache, torch.empty(0, dtype=torch.int64, device=DEV))
+    torch.cuda.synchronize()
+    assert_bitexact(dev.key, rope_oracle.apply_reference(inp.key, inp.positions, inp.cache), "key")
 
 
 def test_nan_and_inf_inputs():
@@ -376,3 +384,39 @@ def test_device_built_tables_drive_the_mirror_kernel():
     q_ref, k_ref = rope_oracle.reference_outputs(inp.query, inp.key, inp.positions, inp.last_index, inp.cache)
     assert_bitexact(dev.query, q_ref, "query")
     assert_bitexact(dev.key, k_ref, "key")
+
+
+@pytest.mark.parametrize("mirror", [False, True])
+def test_large_tile_tables_match_oracle(mirror):
+    """Thousands of short requests: more tiles than the shared-memory table
+    holds, so the slot mapping runs; results must still equal the oracle."""
+    lens = workloads.seeded_uneven_lens(40000, 3000, 9)
+    phase = "prefill_mirror_segmented" if mirror else "segmented_prefill"
+    case = workloads.Case("adhoc_large_table", phase, 40000, 3000 if mirror else 0, lens, flavour="baseline")
+    inp = workloads.make_inputs(case, "cpu")
+    assert inp.num_work_tiles + 1 > 2048
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    dev = run_drop_in(inp, status)
+    q_ref, k_ref = rope_oracle.reference_outputs(inp.query, inp.key, inp.positions, inp.last_index, inp.cache)
+    assert_bitexact(dev.query, q_ref, "query")
+    assert_bitexact(dev.key, k_ref, "key")
+    assert status.item() == 0
+
+
+@pytest.mark.parametrize("pad", [0, 2100])
+def test_non_monotone_tables_are_flagged_and_stay_in_bounds(pad):
+    """A table that runs backwards is outside the reference's contract: the
+    call must flag it and leave lanes 0..191 alone (every access stays inside
+    the K/Q rows by construction)."""
+    n = 300 + pad
+    inp = small_inputs(n, 14)
+    table = list(range(pad)) + [pad + x for x in (0, 64, 32, 96, 300)]
+    starts = torch.tensor(table, dtype=torch.int32, device=DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    dev = inp.to(DEV)
+    welm.rope_prefill(dev.query, dev.key, dev.positions, dev.cache, starts, len(table) - 1, n, 1536, 256, 1,
+                      status=status)
+    torch.cuda.synchronize()
+    assert status.item() & _native.DEV_BAD_TILE
+    assert torch.equal(dev.query.cpu()[..., :192], inp.query[..., :192])
+    assert torch.equal(dev.key.cpu()[..., :192], inp.key[..., :192])

@@ -93,6 +93,8 @@ def test_host_validation_mirror():
     assert mirror(seg=3) == _native.ERR_BAD_MODE
     assert mirror(bs=-1) == _native.ERR_BAD_SIZE
     assert mirror(last=None) == _native.ERR_NULL_POINTER
+    assert mirror(k=None) == _native.ERR_NULL_POINTER
+    assert mirror(q=None, bs=1) == _native.ERR_NULL_POINTER
     assert mirror(bs=2, qs=100) == _native.ERR_BAD_STRIDE
     assert mirror(n=2, ks=8) == _native.ERR_BAD_STRIDE
     assert mirror(seg=1, starts=None) == _native.ERR_NULL_POINTER
