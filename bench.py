@@ -13,10 +13,11 @@ cos/sin cache [16384, 64] (rotary base 1e4), seeded N(0,1) synthetic data.
   replayed from a CUDA graph over 8 rotating buffer sets (270 MB touched
   between reuses, > 126 MB L2) and timed with CUDA events on the launching
   stream; multi-GPU runs take the max time over ranks.
-* ``e2e``: the same metric through the public API with pinned HOST buffers:
-  each step copies Q, K and positions host->device, calls
-  ``welmv4_inplace_rope_npu`` and copies Q and K back, all inside the timed
-  region.
+* ``e2e``: the same metric through the public host-memory API
+  ``welmv4_inplace_rope_host`` with pinned HOST buffers: every step moves
+  the rotated lanes of Q and K and the positions host->device, rotates them
+  and moves the lanes back, chunks pipelined over three streams, all inside
+  the timed region.  The whole-tensor-copy variant is reported beside it.
 * ``roofline``: the op kernel's achieved GB/s (algorithmic bytes per launch
   over the average launch time of the graph-replayed region) against the
   measured HBM copy peak.
@@ -266,8 +267,24 @@ def run_reference_arm(args) -> int:
 # ---------------------------------------------------------------------------
 # GPU arm.
 # ---------------------------------------------------------------------------
+def timed_steps(step, count: int, dist, device, stream) -> float:
+    """Max-over-ranks CUDA-event milliseconds of `count` calls of `step`."""
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize(device)
+    barrier(dist, device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(count):
+        step()
+    end.record(stream)
+    barrier(dist, device)
+    return max_over_ranks(dist, start.elapsed_time(end), device)
+
+
 def run_b200_arm(args) -> int:
     import testfiles_b200 as welm
+    from testfiles_b200 import host as welm_host
     from testfiles_b200 import sharding, workloads
 
     rank, world, local_rank = dist_env()
@@ -337,35 +354,33 @@ def run_b200_arm(args) -> int:
         launches += args.steps
         elapsed_ms = max_over_ranks(dist, start.elapsed_time(end), device)
 
-        # End to end through the public API with pinned host buffers.
+        # End to end through the public host-memory API: Q, K and positions
+        # start in pinned host memory every step and the rotated Q and K end
+        # there (only the rotated lanes cross PCIe; chunks are pipelined).
         e2e_steps = max(1, min(args.steps, args.e2e_steps))
         h_q = host.query.pin_memory()
         h_k = host.key.pin_memory()
         h_p = host.positions.pin_memory()
-        o_q = torch.empty_like(h_q).pin_memory()
-        o_k = torch.empty_like(h_k).pin_memory()
-        d_q, d_k, d_p = torch.empty_like(sets[0][0]), torch.empty_like(sets[0][1]), torch.empty_like(positions)
 
         def e2e_step() -> None:
+            welm_host.welmv4_inplace_rope_host(h_q, h_k, h_p, cache)
+
+        e2e_ms = timed_steps(e2e_step, e2e_steps, dist, device, stream)
+        launches_e2e = e2e_steps * -(-TOKENS // welm_host.DEFAULT_CHUNK_TOKENS)
+
+        # The same through whole-tensor copies (what a caller without the
+        # host API would do), reported beside it.
+        d_q, d_k, d_p = torch.empty_like(sets[0][0]), torch.empty_like(sets[0][1]), torch.empty_like(positions)
+
+        def full_copy_step() -> None:
             d_q.copy_(h_q, non_blocking=True)
             d_k.copy_(h_k, non_blocking=True)
             d_p.copy_(h_p, non_blocking=True)
             welm.welmv4_inplace_rope_npu(d_q, d_k, d_p, cache)
-            o_q.copy_(d_q, non_blocking=True)
-            o_k.copy_(d_k, non_blocking=True)
+            h_q.copy_(d_q, non_blocking=True)
+            h_k.copy_(d_k, non_blocking=True)
 
-        for _ in range(3):
-            e2e_step()
-        torch.cuda.synchronize(device)
-        barrier(dist, device)
-        e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e_start.record(stream)
-        for _ in range(e2e_steps):
-            e2e_step()
-        e_end.record(stream)
-        barrier(dist, device)
-        e2e_ms = max_over_ranks(dist, e_start.elapsed_time(e_end), device)
-        launches_e2e = e2e_steps
+        full_ms = timed_steps(full_copy_step, e2e_steps, dist, device, stream)
     torch.cuda.synchronize(device)
     del body, tail
 
@@ -375,8 +390,8 @@ def run_b200_arm(args) -> int:
     per_launch_gbs = algorithmic_bytes(TOKENS) / per_step_s / 1e9
     peak, peak_kind = hbm_peak()
     e2e_per_step = e2e_ms / 1e3 / e2e_steps
-    h2d = host.query.numel() * 2 + host.key.numel() * 2 + host.positions.numel() * 8
-    d2h = host.query.numel() * 2 + host.key.numel() * 2
+    full_per_step = full_ms / 1e3 / e2e_steps
+    h2d, d2h = welm_host.lane_bytes(TOKENS)
 
     line = None
     if rank == 0:
@@ -431,7 +446,15 @@ def run_b200_arm(args) -> int:
                 "steps": e2e_steps,
                 "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
-                "api": "testfiles_b200.welmv4_inplace_rope_npu (pinned host buffers, copies in the timed region)",
+                "api": "testfiles_b200.welmv4_inplace_rope_host (pinned host Q/K/positions; rotated lanes "
+                       "copied in and out, 2048-token chunks pipelined over 3 streams; copies in the timed region)",
+                "whole_tensor_copies": {
+                    "value": round(total_bytes / full_per_step / 1e9, 3),
+                    "us_per_step": round(full_per_step * 1e6, 2),
+                    "h2d_bytes_per_step": host.query.numel() * 2 + host.key.numel() * 2 + host.positions.numel() * 8,
+                    "d2h_bytes_per_step": host.query.numel() * 2 + host.key.numel() * 2,
+                    "api": "welmv4_inplace_rope_npu on device copies of the whole pinned tensors",
+                },
             },
             "clocks": sampler.summary(),
             "gpu_launches": launches,

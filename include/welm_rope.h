@@ -141,6 +141,22 @@ int welm_rope_build_tiles_host(const int64_t* seq_lens, int64_t batch_size,
                                int32_t* tile_starts, int64_t capacity,
                                int64_t* num_tiles_out, int64_t* last_index_out);
 
+/*
+ * Copies only the rotated lanes (192..255) of `heads` heads of `rows` rows
+ * between host and device memory (direction 0: host -> device, 1: device ->
+ * host): the bytes the op reads and writes, a quarter of every head.  Token
+ * strides are in elements; heads are 256 lanes apart.  Lanes 0..191 of the
+ * destination are not written.  Pinned host memory makes the copy
+ * asynchronous on `stream`.  It is a cudaMemcpy2DAsync per call (one when
+ * both token strides equal heads * 256, else one per head).
+ *
+ * No counterpart in the reference (its Q and K always live on the device); it
+ * serves callers that keep Q/K in host memory and move them per call.
+ */
+int welm_rope_copy_rope_lanes(void* dst, const void* src, int64_t rows, int64_t heads,
+                              int64_t dst_token_stride, int64_t src_token_stride,
+                              int64_t direction, void* stream);
+
 /* Human-readable name of a welm_rope_status code (static storage). */
 const char* welm_rope_status_string(int status);
 

@@ -756,6 +756,40 @@ int welm_rope_build_tiles(const int64_t* seq_lens, int64_t batch_size, int32_t* 
                 device_status);
 }
 
+int welm_rope_copy_rope_lanes(void* dst, const void* src, int64_t rows, int64_t heads,
+                              int64_t dst_token_stride, int64_t src_token_stride, int64_t direction,
+                              void* stream) {
+  if (rows < 0 || heads < 0 || heads > 64) return WELM_ROPE_ERR_BAD_SIZE;
+  if (direction != 0 && direction != 1) return WELM_ROPE_ERR_BAD_MODE;
+  if (rows == 0 || heads == 0) return WELM_ROPE_OK;
+  if (!dst || !src) return WELM_ROPE_ERR_NULL_POINTER;
+  if (rows > 1 && (dst_token_stride < heads * kHeadDim || src_token_stride < heads * kHeadDim))
+    return WELM_ROPE_ERR_BAD_STRIDE;
+  const cudaMemcpyKind kind = direction == 0 ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToHost;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  constexpr size_t kElem = sizeof(uint16_t);
+  constexpr size_t kWidth = size_t(kRopeDim) * kElem;                // 128 bytes per head
+  constexpr size_t kHeadPitch = size_t(kHeadDim) * kElem;            // 512 bytes
+  const size_t lane0 = size_t(kRopeLane0) * kElem;                   // 384 bytes
+  char* d = static_cast<char*>(dst);
+  const char* p = static_cast<const char*>(src);
+  cudaError_t err = cudaSuccess;
+  if ((rows == 1 || (dst_token_stride == heads * kHeadDim && src_token_stride == heads * kHeadDim))) {
+    err = cudaMemcpy2DAsync(d + lane0, kHeadPitch, p + lane0, kHeadPitch, kWidth, size_t(rows * heads), kind, s);
+  } else {
+    for (int64_t h = 0; h < heads && err == cudaSuccess; ++h) {
+      const size_t off = lane0 + size_t(h) * kHeadPitch;
+      err = cudaMemcpy2DAsync(d + off, size_t(dst_token_stride) * kElem, p + off,
+                              size_t(src_token_stride) * kElem, kWidth, size_t(rows), kind, s);
+    }
+  }
+  if (err != cudaSuccess) {
+    cudaGetLastError();
+    return WELM_ROPE_ERR_CUDA;
+  }
+  return WELM_ROPE_OK;
+}
+
 int welm_rope_count_tiles_host(const int64_t* seq_lens, int64_t batch_size,
                                int64_t* num_tiles_out) {
   if (batch_size < 0) return WELM_ROPE_ERR_BAD_SIZE;

@@ -159,3 +159,25 @@ def test_launcher_case_selection_and_fields():
     assert fields["path"] == "kv_mirror" and fields["has_segments"] == 1 and fields["batch_size"] == 128
     assert workloads.min_bytes(cases[0]) == 2056 * 16384
     assert workloads.min_bytes(cases[1]) == 520 * 16384 + 1544 * 128 + 4 * 321
+
+
+def test_copy_rope_lanes_host_validation():
+    lib = _native.load()
+    assert lib.welm_rope_copy_rope_lanes(FAKE, FAKE, -1, 6, 1536, 1536, 0, None) == _native.ERR_BAD_SIZE
+    assert lib.welm_rope_copy_rope_lanes(FAKE, FAKE, 4, 6, 1536, 1536, 2, None) == _native.ERR_BAD_MODE
+    assert lib.welm_rope_copy_rope_lanes(None, FAKE, 4, 6, 1536, 1536, 0, None) == _native.ERR_NULL_POINTER
+    assert lib.welm_rope_copy_rope_lanes(FAKE, FAKE, 4, 6, 1000, 1536, 0, None) == _native.ERR_BAD_STRIDE
+    assert lib.welm_rope_copy_rope_lanes(None, None, 0, 6, 0, 0, 0, None) == _native.OK
+
+
+def test_host_entry_rejects_misuse():
+    import torch
+    from testfiles_b200 import host
+
+    q = torch.zeros((4, 6, 256), dtype=torch.bfloat16)
+    k = torch.zeros((4, 1, 256), dtype=torch.bfloat16)
+    pos = torch.zeros(4, dtype=torch.int64)
+    cache = torch.zeros((8, 64), dtype=torch.float32)
+    with pytest.raises(ValueError):  # the cache selects the device and must be on one
+        host.welmv4_inplace_rope_host(q, k, pos, cache)
+    assert host.lane_bytes(16384) == (16384 * 7 * 128 + 16384 * 8, 16384 * 7 * 128)
