@@ -1,0 +1,94 @@
+"""Request-sharded data parallelism on 2 GPUs (NCCL): each rank rotates its
+shard with the sm_100a op, results are gathered to rank 0 and must equal the
+oracle on the unsharded batch bit for bit.  Needs two visible GPUs."""
+
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank: int, world: int, port: int, queue) -> None:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    results = {}
+    try:
+        import testfiles_b200 as welm
+        from oracle import rope_oracle
+        from testfiles_b200 import sharding, workloads
+
+        # segmented KV mirror, sharded by whole requests
+        case = workloads.find_case("b_mirror_segmented_n16384_bs128_uneven")
+        full = workloads.make_inputs(case, "cpu")
+        lens = case.segment_lens
+        ranges = sharding.shard_requests(lens, world)
+        local = sharding.local_batch(lens, ranges[rank], full.last_index.tolist())
+        r0, r1 = ranges[rank]
+        t0, t1 = local.token_begin, local.token_end
+        q = full.query[r0:r1].to(dev)
+        k = full.key[t0:t1].to(dev)
+        pos = full.positions[t0:t1].to(dev)
+        last = torch.tensor(local.last_index, dtype=torch.int64, device=dev)
+        starts = torch.tensor(local.tile_starts, dtype=torch.int32, device=dev)
+        welm.welmv4_inplace_rope_npu(q, k, pos, full.cache.to(dev), last, starts)
+        k_counts = [sharding.local_batch(lens, rr).n_tokens for rr in ranges]
+        q_counts = [rr[1] - rr[0] for rr in ranges]
+        k_all = sharding.gather_rows(k, k_counts)
+        q_all = sharding.gather_rows(q, q_counts)
+        if rank == 0:
+            q_ref, k_ref = rope_oracle.reference_outputs(full.query, full.key, full.positions, full.last_index,
+                                                         full.cache)
+            results["mirror"] = (torch.equal(q_all.cpu().view(torch.int16), q_ref.view(torch.int16)),
+                                 torch.equal(k_all.cpu().view(torch.int16), k_ref.view(torch.int16)))
+
+        # ordinary prefill, sharded by 64-aligned token ranges
+        case = workloads.find_case("b_prefill_m9616")
+        full = workloads.make_inputs(case, "cpu")
+        a, b = sharding.shard_tokens(case.n_tokens, world, rank)
+        q = full.query[a:b].to(dev)
+        k = full.key[a:b].to(dev)
+        welm.welmv4_inplace_rope_npu(q, k, full.positions[a:b].to(dev), full.cache.to(dev))
+        counts = [sharding.shard_tokens(case.n_tokens, world, r)[1] - sharding.shard_tokens(case.n_tokens, world, r)[0]
+                  for r in range(world)]
+        q_all = sharding.gather_rows(q, counts)
+        k_all = sharding.gather_rows(k, counts)
+        if rank == 0:
+            q_ref, k_ref = rope_oracle.reference_outputs(full.query, full.key, full.positions, None, full.cache)
+            results["prefill"] = (torch.equal(q_all.cpu().view(torch.int16), q_ref.view(torch.int16)),
+                                  torch.equal(k_all.cpu().view(torch.int16), k_ref.view(torch.int16)))
+            queue.put(results)
+        dist.barrier(device_ids=[rank])
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_gpu_request_sharding_matches_oracle():
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, queue)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = queue.get(timeout=240)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert results == {"mirror": (True, True), "prefill": (True, True)}
