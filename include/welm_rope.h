@@ -50,7 +50,8 @@ typedef enum welm_rope_status {
   WELM_ROPE_ERR_BAD_SIZE = 3,     /* negative or too large N / BS / tiles / P     */
   WELM_ROPE_ERR_BAD_STRIDE = 4,   /* token stride makes rows overlap              */
   WELM_ROPE_ERR_CAPACITY = 5,     /* output buffer too small (tile builder)       */
-  WELM_ROPE_ERR_CUDA = 6          /* the CUDA runtime refused the launch          */
+  WELM_ROPE_ERR_CUDA = 6,         /* the CUDA runtime refused the launch          */
+  WELM_ROPE_ERR_TOO_MANY_TOKENS = 7 /* more tokens than the static staging area holds */
 } welm_rope_status;
 
 /* Device-side status bits (ORed into *device_status when it is non-NULL). */
@@ -156,6 +157,40 @@ int welm_rope_build_tiles_host(const int64_t* seq_lens, int64_t batch_size,
 int welm_rope_copy_rope_lanes(void* dst, const void* src, int64_t rows, int64_t heads,
                               int64_t dst_token_stride, int64_t src_token_stride,
                               int64_t direction, void* stream);
+
+/*
+ * Ordinary prefill / decode RoPE on Q/K held in host memory, without any
+ * allocation: for callers that cannot allocate device memory — a plugin whose
+ * host process owns every byte of device memory through its own allocator, or
+ * code on a latency-critical path where cudaMalloc/cudaFree (which may
+ * synchronise the device) are not allowed.  The rotated lanes of Q
+ * [n_tokens, 6, 256] and K [n_tokens, 1, 256] and the positions are staged
+ * through a fixed area inside this library (a static device array of
+ * WELM_ROPE_STATIC_MAX_TOKENS tokens, about 1.85 MB, which every GPU that
+ * loads the library holds until the process exits), rotated there and copied
+ * back, all on `stream`; lanes 0..191 of Q and K are never written.  q, k and
+ * positions may be host (pinned for asynchronous copies) or device memory;
+ * cos_sin_cache is device memory.  More than WELM_ROPE_STATIC_MAX_TOKENS
+ * tokens is rejected with WELM_ROPE_ERR_TOO_MANY_TOKENS (split larger batches
+ * into several calls).
+ *
+ * The first call on each device looks up the staging area's device address
+ * (cudaGetSymbolAddress, with that device current); make that first call
+ * before any stream capture.  Every call shares the one staging area: calls
+ * whose work overlaps on the GPU (different streams, or different host
+ * threads without ordering) race on it and must be serialised by the caller.
+ * The area is fully rewritten by each call before it is read, so the previous
+ * call's leftovers never reach a result.
+ *
+ * No counterpart in the reference: it keeps Q and K on the device and
+ * allocates freely.
+ */
+#define WELM_ROPE_STATIC_MAX_TOKENS 2048
+int welm_rope_ordinary_host_static(void* q, void* k, const int64_t* positions,
+                                   const float* cos_sin_cache, int64_t n_tokens,
+                                   int64_t q_token_stride, int64_t k_token_stride,
+                                   int64_t max_position, int32_t* device_status,
+                                   void* stream);
 
 /* Human-readable name of a welm_rope_status code (static storage). */
 const char* welm_rope_status_string(int status);

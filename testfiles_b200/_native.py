@@ -21,6 +21,8 @@ ERR_BAD_SIZE = 3
 ERR_BAD_STRIDE = 4
 ERR_CAPACITY = 5
 ERR_CUDA = 6
+ERR_TOO_MANY_TOKENS = 7
+STATIC_MAX_TOKENS = 2048
 
 # Device status bits.
 DEV_BAD_POSITION = 1
@@ -37,6 +39,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "welm_rope_mirror": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P]),
     "welm_rope_build_tiles": (ctypes.c_int, [_P, _I64, _P, _I64, _P, _P, _P, _P]),
     "welm_rope_copy_rope_lanes": (ctypes.c_int, [_P, _P, _I64, _I64, _I64, _I64, _I64, _P]),
+    "welm_rope_ordinary_host_static": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _P]),
     "welm_rope_count_tiles_host": (ctypes.c_int, [_P, _I64, _P]),
     "welm_rope_build_tiles_host": (ctypes.c_int, [_P, _I64, _P, _I64, _P, _P]),
     "welm_rope_status_string": (ctypes.c_char_p, [ctypes.c_int]),

@@ -538,6 +538,59 @@ build_tiles_kernel(const int64_t* __restrict__ lens, int32_t bs, int32_t* __rest
 }
 
 // ---------------------------------------------------------------------------
+// Allocation-free host entry (welm_rope_ordinary_host_static): a static staging
+// area in device memory holds the rope lanes of up to kStaticTokens tokens in
+// a compact layout — Q [tokens][6][64], K [tokens][64] (bf16) — plus their
+// positions.  Host code must not use the array's name as an address (it is a
+// host-side stand-in); it looks the device address up once per device.
+// ---------------------------------------------------------------------------
+constexpr int kStaticTokens = WELM_ROPE_STATIC_MAX_TOKENS;
+constexpr size_t kStageQBytes = size_t(kStaticTokens) * kQHeads * kRopeDim * sizeof(uint16_t);
+constexpr size_t kStageKBytes = size_t(kStaticTokens) * kRopeDim * sizeof(uint16_t);
+constexpr size_t kStagePosBytes = size_t(kStaticTokens) * sizeof(int64_t);
+constexpr size_t kStageBytes = kStageQBytes + kStageKBytes + kStagePosBytes;
+
+static __device__ __align__(256) unsigned char g_static_stage[kStageBytes];
+
+// Rotates staged rows: one item = (token, part) as in the other kernels, over
+// the compact staging layout (head stride 64, rope lanes from 0).
+__global__ void __launch_bounds__(kBlock)
+rope_staged_kernel(uint16_t* q, uint16_t* k, const int64_t* positions, const float* cache,
+                   int32_t items, int64_t max_position, int32_t* status) {
+  pdl_enter();
+  const int stride = gridDim.x * blockDim.x;
+  for (int item = blockIdx.x * blockDim.x + threadIdx.x; item < items; item += stride) {
+    const int part = item & (kParts - 1);
+    const int tok = item >> kPartShift;
+    const int64_t pos = __ldg(positions + tok);
+    uint16_t* kb = k + size_t(tok) * kRopeDim + part * kLanes;
+    uint16_t* qb = q + size_t(tok) * kQHeads * kRopeDim + part * kLanes;
+    uint4 kx1 = Io<true>::load8(kb), kx2 = Io<true>::load8(kb + kHalf);
+    uint4 qx1[kQHeads], qx2[kQHeads];
+#pragma unroll
+    for (int h = 0; h < kQHeads; ++h) {
+      qx1[h] = Io<true>::load8(qb + h * kRopeDim);
+      qx2[h] = Io<true>::load8(qb + h * kRopeDim + kHalf);
+    }
+    if (pos < 0 || pos >= max_position) {
+      if (part == 0) raise_status(status, WELM_ROPE_DEV_BAD_POSITION);
+      continue;  // the staged lanes go back unchanged
+    }
+    CosSin cs;
+    Io<true>::load_cos_sin(cache + pos * kRopeDim, part, cs);
+    rotate8(kx1, kx2, cs);
+    Io<true>::store8(kb, kx1);
+    Io<true>::store8(kb + kHalf, kx2);
+#pragma unroll
+    for (int h = 0; h < kQHeads; ++h) {
+      rotate8(qx1[h], qx2[h], cs);
+      Io<true>::store8(qb + h * kRopeDim, qx1[h]);
+      Io<true>::store8(qb + h * kRopeDim + kHalf, qx2[h]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side.
 // ---------------------------------------------------------------------------
 constexpr int64_t kMaxItems = int64_t(1) << 30;  // item indices stay in int32
@@ -646,6 +699,52 @@ int launch_mirror(const Plan& plan, const RopeArgs& a, cudaStream_t s) {
   }
 }
 
+// Device address of g_static_stage on the current device, looked up once per
+// device (with that device current) and cached; nullptr if the lookup fails.
+unsigned char* static_stage_for_current_device() {
+  static std::atomic<unsigned char*> cache[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  unsigned char* p = cache[dev].load(std::memory_order_acquire);
+  if (p != nullptr) return p;
+  void* addr = nullptr;
+  if (cudaGetSymbolAddress(&addr, g_static_stage) != cudaSuccess || addr == nullptr) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  p = static_cast<unsigned char*>(addr);
+  cache[dev].store(p, std::memory_order_release);
+  return p;
+}
+
+// Copies the rope lanes of `heads` heads of `rows` rows between a full-layout
+// tensor (token stride `full_stride` elements, heads 256 apart) and the
+// compact staging layout (rows of heads x 64 lanes).
+cudaError_t copy_compact(void* compact, void* full, int64_t rows, int heads, int64_t full_stride,
+                         bool to_stage, cudaStream_t s) {
+  constexpr size_t kElem = sizeof(uint16_t);
+  constexpr size_t kWidth = size_t(kRopeDim) * kElem;  // 128 bytes
+  char* c = static_cast<char*>(compact);
+  char* f = static_cast<char*>(full) + size_t(kRopeLane0) * kElem;
+  if (rows == 1 || full_stride == int64_t(heads) * kHeadDim) {  // one 2D copy over rows * heads
+    const size_t fp = size_t(kHeadDim) * kElem;
+    return to_stage ? cudaMemcpy2DAsync(c, kWidth, f, fp, kWidth, size_t(rows * heads), cudaMemcpyDefault, s)
+                    : cudaMemcpy2DAsync(f, fp, c, kWidth, kWidth, size_t(rows * heads), cudaMemcpyDefault, s);
+  }
+  const size_t cp = kWidth * size_t(heads), fp = size_t(full_stride) * kElem;
+  for (int h = 0; h < heads; ++h) {
+    char* ch = c + size_t(h) * kWidth;
+    char* fh = f + size_t(h) * kHeadDim * kElem;
+    const cudaError_t e = to_stage ? cudaMemcpy2DAsync(ch, cp, fh, fp, kWidth, size_t(rows), cudaMemcpyDefault, s)
+                                   : cudaMemcpy2DAsync(fh, fp, ch, cp, kWidth, size_t(rows), cudaMemcpyDefault, s);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
 }  // namespace
 
 extern "C" {
@@ -661,6 +760,8 @@ const char* welm_rope_status_string(int status) {
     case WELM_ROPE_ERR_BAD_STRIDE: return "token stride makes rows overlap";
     case WELM_ROPE_ERR_CAPACITY: return "output buffer too small";
     case WELM_ROPE_ERR_CUDA: return "CUDA launch failed";
+    case WELM_ROPE_ERR_TOO_MANY_TOKENS:
+      return "n_tokens exceeds WELM_ROPE_STATIC_MAX_TOKENS (2048) of the static staging area; split the batch";
     default: return "unknown welm_rope status";
   }
 }
@@ -784,6 +885,43 @@ int welm_rope_copy_rope_lanes(void* dst, const void* src, int64_t rows, int64_t 
     }
   }
   if (err != cudaSuccess) {
+    cudaGetLastError();
+    return WELM_ROPE_ERR_CUDA;
+  }
+  return WELM_ROPE_OK;
+}
+
+int welm_rope_ordinary_host_static(void* q, void* k, const int64_t* positions, const float* cos_sin_cache,
+                                   int64_t n_tokens, int64_t q_token_stride, int64_t k_token_stride,
+                                   int64_t max_position, int32_t* device_status, void* stream) {
+  if (n_tokens < 0 || max_position < 0) return WELM_ROPE_ERR_BAD_SIZE;
+  if (n_tokens > kStaticTokens) return WELM_ROPE_ERR_TOO_MANY_TOKENS;
+  if (n_tokens == 0) return WELM_ROPE_OK;
+  if (!q || !k || !positions || !cos_sin_cache) return WELM_ROPE_ERR_NULL_POINTER;
+  if (n_tokens > 1 && (q_token_stride < kQHeads * kHeadDim || k_token_stride < kHeadDim))
+    return WELM_ROPE_ERR_BAD_STRIDE;
+  if (!aligned16(cos_sin_cache)) return WELM_ROPE_ERR_BAD_STRIDE;  // the staged kernel reads 16-byte vectors
+  unsigned char* stage = static_stage_for_current_device();
+  if (stage == nullptr) return WELM_ROPE_ERR_CUDA;
+  uint16_t* sq = reinterpret_cast<uint16_t*>(stage);
+  uint16_t* sk = reinterpret_cast<uint16_t*>(stage + kStageQBytes);
+  int64_t* sp = reinterpret_cast<int64_t*>(stage + kStageQBytes + kStageKBytes);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = copy_compact(sq, q, n_tokens, kQHeads, q_token_stride, true, s);
+  if (e == cudaSuccess) e = copy_compact(sk, k, n_tokens, 1, k_token_stride, true, s);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(sp, positions, size_t(n_tokens) * sizeof(int64_t), cudaMemcpyDefault, s);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return WELM_ROPE_ERR_CUDA;
+  }
+  const int32_t items = int32_t(n_tokens * kParts);
+  const int rc = launch(rope_staged_kernel, unsigned((items + kBlock - 1) / kBlock), kBlock, 0, s, sq, sk,
+                        static_cast<const int64_t*>(sp), cos_sin_cache, items, max_position, device_status);
+  if (rc != WELM_ROPE_OK) return rc;
+  e = copy_compact(sq, q, n_tokens, kQHeads, q_token_stride, false, s);
+  if (e == cudaSuccess) e = copy_compact(sk, k, n_tokens, 1, k_token_stride, false, s);
+  if (e != cudaSuccess) {
     cudaGetLastError();
     return WELM_ROPE_ERR_CUDA;
   }

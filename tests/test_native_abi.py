@@ -181,3 +181,16 @@ def test_host_entry_rejects_misuse():
     with pytest.raises(ValueError):  # the cache selects the device and must be on one
         host.welmv4_inplace_rope_host(q, k, pos, cache)
     assert host.lane_bytes(16384) == (16384 * 7 * 128 + 16384 * 8, 16384 * 7 * 128)
+
+
+def test_static_host_entry_rejects_oversized_batches_before_any_cuda_call():
+    lib = _native.load()
+    rc = lib.welm_rope_ordinary_host_static(FAKE, FAKE, FAKE, FAKE, _native.STATIC_MAX_TOKENS + 1, 1536, 256, 16,
+                                            None, None)
+    assert rc == _native.ERR_TOO_MANY_TOKENS
+    assert "2048" in _native.status_string(rc)
+    assert lib.welm_rope_ordinary_host_static(FAKE, FAKE, FAKE, FAKE, -1, 1536, 256, 16, None, None) == \
+        _native.ERR_BAD_SIZE
+    assert lib.welm_rope_ordinary_host_static(None, FAKE, FAKE, FAKE, 4, 1536, 256, 16, None, None) == \
+        _native.ERR_NULL_POINTER
+    assert lib.welm_rope_ordinary_host_static(None, None, None, None, 0, 0, 0, 0, None, None) == _native.OK
