@@ -112,6 +112,32 @@ int welm_rope_mirror(void* q, void* k, const int64_t* positions,
                      int32_t* device_status, void* stream);
 
 /*
+ * Segmented KV-mirror prefill driven directly by request lengths on the
+ * device: no tile table, no last_index tensor and no host round trip between
+ * building them and launching.  Request r holds seq_lens[r] consecutive K
+ * tokens; K token t < sum(seq_lens) is rotated at positions[t] (the
+ * reference's per-request 64-token tiles cover every token of every request);
+ * Q row r is rotated at positions[end_r - 1] with end_r = seq_lens[0] + ... +
+ * seq_lens[r] (the reference's segmented last_index).  The result equals
+ * welm_rope_build_tiles followed by welm_rope_mirror with has_segments = 1.
+ * Negative lengths count as 0 and raise WELM_ROPE_DEV_BAD_LENGTH; tokens at or
+ * past min(N, sum) are not touched; a Q row whose end_r is 0 or past N raises
+ * WELM_ROPE_DEV_BAD_LAST_INDEX and is skipped.  batch_size <=
+ * WELM_ROPE_LENS_MAX_BATCH (the lengths are staged in shared memory).
+ *
+ * Row 4 of the path's "next" list (on-device tile building fused with the
+ * mirror launch); the reference builds tiles on the host
+ * (bench_welmv4_inplace_rope_npu.py:1439-1461) before each launch.
+ */
+#define WELM_ROPE_LENS_MAX_BATCH 2048
+int welm_rope_mirror_from_lens(void* q, void* k, const int64_t* positions,
+                               const float* cos_sin_cache, const int64_t* seq_lens,
+                               int64_t n_tokens, int64_t batch_size,
+                               int64_t q_token_stride, int64_t k_token_stride,
+                               int64_t max_position, int32_t* device_status,
+                               void* stream);
+
+/*
  * Segmented 64-token tile-boundary builder on the device.  For request r of
  * length len_r starting at token off_r it emits off_r, off_r+64, ... (< off_r
  * + len_r), then the final total N: int32 starts[T+1], T = sum ceil(len_r/64).

@@ -16,11 +16,13 @@ from .ops import (  # noqa: F401
     build_segment_tile_starts,
     build_segment_tile_starts_device,
     count_segment_tiles,
+    rope_mirror_from_lens,
     rope_mirror_prefill,
     rope_prefill,
     segment_placeholder,
     welmv4_inplace_rope,
     welmv4_inplace_rope_npu,
 )
+from .host import welmv4_inplace_rope_host  # noqa: F401,E402
 
 __version__ = "0.1.0"

@@ -23,6 +23,7 @@ ERR_CAPACITY = 5
 ERR_CUDA = 6
 ERR_TOO_MANY_TOKENS = 7
 STATIC_MAX_TOKENS = 2048
+LENS_MAX_BATCH = 2048
 
 # Device status bits.
 DEV_BAD_POSITION = 1
@@ -37,6 +38,7 @@ _I64 = ctypes.c_int64
 SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "welm_rope_ordinary": (ctypes.c_int, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P]),
     "welm_rope_mirror": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P]),
+    "welm_rope_mirror_from_lens": (ctypes.c_int, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P]),
     "welm_rope_build_tiles": (ctypes.c_int, [_P, _I64, _P, _I64, _P, _P, _P, _P]),
     "welm_rope_copy_rope_lanes": (ctypes.c_int, [_P, _P, _I64, _I64, _I64, _I64, _I64, _P]),
     "welm_rope_ordinary_host_static": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _P]),

@@ -446,6 +446,94 @@ __global__ void __launch_bounds__(kBlock) rope_mirror_kernel(const RopeArgs a) {
 }
 
 // ---------------------------------------------------------------------------
+// KV mirror from request lengths.  Every CTA stages the BS lengths into shared
+// memory (cp.async) while its K-token loads and cache gathers fly; after the
+// one barrier each warp derives what it needs with shuffles, without further
+// CTA-wide synchronisation: K token t is rotated iff t < sum(lengths), Q row
+// r uses src = end_r - 1 with end_r = lengths[0] + ... + lengths[r].  One
+// item per thread: Q rows, then K tokens.
+// ---------------------------------------------------------------------------
+constexpr int kLensCap = WELM_ROPE_LENS_MAX_BATCH;
+
+// Warp-cooperative prefix over the staged lengths (negative entries count as
+// 0): returns the total and, for `row` in [0, n), end_row = s[0] + ... +
+// s[row].  Every lane of the warp must call it (it shuffles).
+__device__ __forceinline__ int64_t warp_request_ends(const int64_t* s, int n, int row, int64_t& end_row,
+                                                     bool& negative) {
+  const int lane = threadIdx.x & 31;
+  const int chunk = (n + 31) >> 5;
+  const int lo = min(n, lane * chunk), hi = min(n, lo + chunk);
+  int64_t part_sum = 0;
+  for (int i = lo; i < hi; ++i) {
+    const int64_t v = s[i];
+    negative |= v < 0;
+    part_sum += v > 0 ? v : 0;
+  }
+  negative = __any_sync(0xffffffffu, negative);
+  int64_t incl = part_sum;  // inclusive scan of the lanes' chunk sums
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int64_t t = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += t;
+  }
+  const int64_t total = __shfl_sync(0xffffffffu, incl, 31);
+  const int c = row >= 0 && row < n ? row / chunk : 0;  // the chunk holding `row`
+  const int64_t before = __shfl_sync(0xffffffffu, incl - part_sum, c);
+  end_row = before;
+  if (row >= 0 && row < n) {
+    for (int i = c * chunk; i <= row; ++i) {
+      const int64_t v = s[i];
+      end_row += v > 0 ? v : 0;
+    }
+  }
+  return total;
+}
+
+// At most 128 registers, so 4 CTAs fit per SM and a 16384-token launch
+// (516 CTAs) stays resident in one wave on 148 SMs.
+template <bool kVec>
+__global__ void __launch_bounds__(kBlock, 4) rope_mirror_lens_kernel(const RopeArgs a, const int64_t* lens, int batch) {
+  extern __shared__ int64_t s_len[];
+  pdl_enter();
+  for (int j = threadIdx.x; j < batch; j += blockDim.x) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(s_len + j)), "l"(lens + j) : "memory");
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  const int item = blockIdx.x * blockDim.x + threadIdx.x;
+  const int part = item & (kParts - 1);
+  const bool is_q = item < a.q_items;
+  const int k_item = item - a.q_items;
+  const bool is_token = !is_q && k_item < a.k_items;
+  const int64_t tok = is_token ? (k_item >> kPartShift) : 0;
+  Slices<kVec, kQHeads> qx;
+  Slices<kVec, 1> kx;
+  CosSin cs;
+  bool pos_ok = false;
+  if (is_q) {
+    qx.load(a.q + int64_t(item >> kPartShift) * a.q_stride, part);
+  } else if (is_token) {
+    const int64_t pos = __ldg(a.positions + tok);
+    kx.load(a.k + tok * a.k_stride, part);
+    pos_ok = gather_cos_sin<kVec>(a, pos, part, cs);
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
+  int64_t end_row = 0;
+  bool negative = false;
+  const int64_t total = warp_request_ends(s_len, batch, is_q ? (item >> kPartShift) : -1, end_row, negative);
+  if (is_q) {
+    finish_q_row<kVec>(a, qx, end_row - 1, part);
+  } else if (is_token && tok < total) {
+    if (pos_ok) {
+      kx.rotate_store(cs);
+    } else if (part == 0) {
+      raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
+    }
+  }
+  if (negative && blockIdx.x == 0 && threadIdx.x == 0) raise_status(a.status, WELM_ROPE_DEV_BAD_LENGTH);
+}
+
+// ---------------------------------------------------------------------------
 // Segmented tile-boundary builder: one CTA, requests processed in chunks of
 // kBuildThreads with a running carry (tokens, tiles).  Within a chunk the
 // per-request tile counts and lengths are scanned with warp shuffles, then the
@@ -843,6 +931,40 @@ int welm_rope_mirror(void* q, void* k, const int64_t* positions, const float* co
                    (n_tokens <= 1 || k_token_stride % 8 == 0);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return vec ? launch_mirror<true>(plan, a, s) : launch_mirror<false>(plan, a, s);
+}
+
+int welm_rope_mirror_from_lens(void* q, void* k, const int64_t* positions, const float* cos_sin_cache,
+                               const int64_t* seq_lens, int64_t n_tokens, int64_t batch_size,
+                               int64_t q_token_stride, int64_t k_token_stride, int64_t max_position,
+                               int32_t* device_status, void* stream) {
+  if (n_tokens < 0 || batch_size < 0 || max_position < 0) return WELM_ROPE_ERR_BAD_SIZE;
+  if (batch_size > kLensCap || n_tokens > kMaxItems / kParts - kLensCap) return WELM_ROPE_ERR_BAD_SIZE;
+  if (batch_size == 0 || n_tokens == 0) return WELM_ROPE_OK;  // no request, or no token to rotate
+  if (!q || !k || !positions || !cos_sin_cache || !seq_lens) return WELM_ROPE_ERR_NULL_POINTER;
+  if ((batch_size > 1 && q_token_stride < kQHeads * kHeadDim) || (n_tokens > 1 && k_token_stride < kHeadDim))
+    return WELM_ROPE_ERR_BAD_STRIDE;
+  if ((reinterpret_cast<uintptr_t>(seq_lens) & 7u) != 0) return WELM_ROPE_ERR_BAD_STRIDE;  // 8-byte cp.async
+  RopeArgs a{};
+  a.q = static_cast<uint16_t*>(q);
+  a.k = static_cast<uint16_t*>(k);
+  a.positions = positions;
+  a.cache = cos_sin_cache;
+  a.q_stride = q_token_stride;
+  a.k_stride = k_token_stride;
+  a.n_tokens = n_tokens;
+  a.max_position = max_position;
+  a.status = device_status;
+  a.q_items = int32_t(batch_size * kParts);
+  a.k_items = int32_t(n_tokens * kParts);
+  const bool vec = aligned16(q) && aligned16(k) && aligned16(cos_sin_cache) &&
+                   (batch_size <= 1 || q_token_stride % 8 == 0) && (n_tokens <= 1 || k_token_stride % 8 == 0);
+  const int64_t total = int64_t(a.q_items) + a.k_items;
+  const unsigned grid = unsigned((total + kBlock - 1) / kBlock);
+  const size_t smem = size_t(batch_size) * sizeof(int64_t);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int b = int(batch_size);
+  return vec ? launch(rope_mirror_lens_kernel<true>, grid, kBlock, smem, s, a, seq_lens, b)
+             : launch(rope_mirror_lens_kernel<false>, grid, kBlock, smem, s, a, seq_lens, b);
 }
 
 int welm_rope_build_tiles(const int64_t* seq_lens, int64_t batch_size, int32_t* tile_starts,

@@ -84,13 +84,24 @@ def select_cases(spec: str) -> list[workloads.Case]:
 
 
 def _launch(inp: workloads.Inputs) -> None:
+    lens = inp.extra.get("seq_lens")
+    if lens is not None:  # segmented KV mirror straight from request lengths
+        ops.rope_mirror_from_lens(inp.query, inp.key, inp.positions, inp.cache, lens)
+        return
     ops.welmv4_inplace_rope_npu(inp.query, inp.key, inp.positions, inp.cache, inp.last_index,
                                 inp.segment_tile_starts)
 
 
+def _with_lens(case: workloads.Case, inp: workloads.Inputs, device: torch.device) -> workloads.Inputs:
+    if case.is_mirror and case.is_segmented:
+        inp.extra["seq_lens"] = torch.tensor(case.segment_lens, dtype=torch.int64, device=device)
+    return inp
+
+
 def time_case(case: workloads.Case, device: torch.device, trials: int = 5, graph_launches: int = 64,
-              replays: Optional[int] = None) -> dict:
-    """µs per launch of ``case`` (graph-replayed over rotating buffer sets)."""
+              replays: Optional[int] = None, from_lens: bool = False) -> dict:
+    """µs per launch of ``case`` (graph-replayed over rotating buffer sets);
+    ``from_lens`` runs segmented mirror cases through rope_mirror_from_lens."""
     host = workloads.make_inputs(case, "cpu")
     nbytes = workloads.min_bytes(case)
     sets_needed = max(2, -(-2 * L2_BYTES // max(nbytes, 1)))
@@ -101,6 +112,8 @@ def time_case(case: workloads.Case, device: torch.device, trials: int = 5, graph
         b = base.clone()
         b.positions = base.positions.clone()
         b.cache = base.cache.clone()
+        if from_lens:
+            _with_lens(case, b, device)
         buffers.append(b)
     for i in range(3):
         _launch(buffers[i % sets])
@@ -143,14 +156,18 @@ def time_case(case: workloads.Case, device: torch.device, trials: int = 5, graph
         "buffer_sets": sets,
         "l2_cold": bool(sets * nbytes > 2 * L2_BYTES),
         "pdl": os.environ.get("WELM_ROPE_PDL", "1") != "0",
+        "entry": "rope_mirror_from_lens" if from_lens and case.is_mirror and case.is_segmented
+        else "welmv4_inplace_rope_npu",
         "device_name": torch.cuda.get_device_name(device),
         "torch_version": torch.__version__,
         "python_version": platform.python_version(),
     }
 
 
-def launch_case(case: workloads.Case, device: torch.device, iters: int) -> dict:
+def launch_case(case: workloads.Case, device: torch.device, iters: int, from_lens: bool = False) -> dict:
     inp = workloads.make_inputs(case, device)
+    if from_lens:
+        _with_lens(case, inp, device)
     for _ in range(iters):
         _launch(inp)
     torch.cuda.synchronize(device)
@@ -159,12 +176,13 @@ def launch_case(case: workloads.Case, device: torch.device, iters: int) -> dict:
 
 
 def run(cases: Iterable[workloads.Case], device: torch.device, time_it: bool, iters: int,
-        out: Optional[str]) -> list[dict]:
+        out: Optional[str], from_lens: bool = False) -> list[dict]:
     records = []
     sink = open(out, "a") if out else None
     try:
         for case in cases:
-            rec = time_case(case, device) if time_it else launch_case(case, device, iters)
+            rec = (time_case(case, device, from_lens=from_lens) if time_it
+                   else launch_case(case, device, iters, from_lens))
             records.append(rec)
             line = json.dumps(rec)
             print(line, flush=True)
@@ -185,13 +203,15 @@ def main(argv: Optional[list[str]] = None) -> int:
     parser.add_argument("--iters", type=int, default=20, help="eager launches per case (without --time)")
     parser.add_argument("--device", default="cuda:0")
     parser.add_argument("--json", default=None, help="append JSON lines here")
+    parser.add_argument("--mirror-from-lens", action="store_true",
+                        help="run segmented KV-mirror cases through rope_mirror_from_lens")
     args = parser.parse_args(argv)
     if not torch.cuda.is_available():
         print("the launcher needs a CUDA device", file=sys.stderr)
         return 2
     device = torch.device(args.device)
     torch.cuda.set_device(device)
-    run(select_cases(args.cases), device, args.time, args.iters, args.json)
+    run(select_cases(args.cases), device, args.time, args.iters, args.json, args.mirror_from_lens)
     return 0
 
 

@@ -49,6 +49,7 @@ __all__ = [
     "welmv4_inplace_rope",
     "rope_prefill",
     "rope_mirror_prefill",
+    "rope_mirror_from_lens",
     "build_segment_tile_starts",
     "build_segment_tile_starts_device",
     "count_segment_tiles",
@@ -232,6 +233,36 @@ def welmv4_inplace_rope_npu(
 
 
 welmv4_inplace_rope = welmv4_inplace_rope_npu
+
+
+def rope_mirror_from_lens(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    positions: torch.Tensor,
+    cos_sin_cache: torch.Tensor,
+    seq_lens: torch.Tensor,
+    status: Optional[torch.Tensor] = None,
+) -> None:
+    """Segmented KV-mirror prefill from device request lengths (no tile table,
+    no last_index, no host round trip): K token t < sum(seq_lens) at
+    positions[t]; Q row r at positions[seq_lens[0] + ... + seq_lens[r] - 1].
+    Equals build_segment_tile_starts_device + rope_mirror_prefill."""
+    device = _check_common(q, k, positions, cos_sin_cache)
+    _require(seq_lens, "seq_lens", torch.int64, device)
+    if seq_lens.dim() != 1 or (seq_lens.numel() > 1 and seq_lens.stride(0) != 1):
+        raise ValueError("seq_lens must be a contiguous 1-D int64 tensor")
+    batch = int(seq_lens.numel())
+    if batch > _native.LENS_MAX_BATCH:
+        raise ValueError(f"at most {_native.LENS_MAX_BATCH} requests per call")
+    if q.shape[0] != batch:
+        raise ValueError("query needs one row per request")
+    n = int(positions.shape[0])
+    if k.shape[0] != n:
+        raise ValueError("key rows must equal the positions length")
+    rc = _native.load().welm_rope_mirror_from_lens(
+        _ptr(q), _ptr(k), _ptr(positions), _ptr(cos_sin_cache), _ptr(seq_lens), n, batch, int(q.stride(0)),
+        int(k.stride(0)), int(cos_sin_cache.shape[0]), _status_ptr(status, device), _stream(device))
+    _native.check("welm_rope_mirror_from_lens", rc)
 
 
 # ---------------------------------------------------------------------------

@@ -420,3 +420,47 @@ def test_non_monotone_tables_are_flagged_and_stay_in_bounds(pad):
     assert status.item() & _native.DEV_BAD_TILE
     assert torch.equal(dev.query.cpu()[..., :192], inp.query[..., :192])
     assert torch.equal(dev.key.cpu()[..., :192], inp.key[..., :192])
+
+
+# ---------------------------------------------------------------------------
+# KV mirror straight from request lengths (no tile table, no last_index).
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("lens", [
+    [16384], [4096, 4096], list(workloads.seeded_uneven_lens(16384, 128, 4)), [1] * 2048,
+    [0, 5, 0, 64, 65, 1, 0, 300], list(workloads.reference_uneven_lens(9616, 8)),
+])
+def test_mirror_from_lens_matches_oracle(lens):
+    n = sum(lens)
+    case = workloads.Case("adhoc_lens", "prefill_mirror_segmented", n, len(lens), tuple(lens), flavour="baseline")
+    inp = workloads.make_inputs(case, "cpu")
+    dev = inp.to(DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    welm.rope_mirror_from_lens(dev.query, dev.key, dev.positions, dev.cache,
+                               torch.tensor(lens, dtype=torch.int64, device=DEV), status=status)
+    torch.cuda.synchronize()
+    ends = torch.tensor(lens).cumsum(0)
+    valid_q = ends > 0  # a leading zero-length request has no last token
+    q_ref = rope_oracle.apply_reference(inp.query[valid_q], inp.positions[ends[valid_q] - 1], inp.cache)
+    k_ref = rope_oracle.apply_reference(inp.key, inp.positions, inp.cache)
+    assert_bitexact(dev.query.cpu()[valid_q], q_ref, "query")
+    assert torch.equal(dev.query.cpu()[~valid_q], inp.query[~valid_q])
+    assert_bitexact(dev.key, k_ref, "key")
+    assert status.item() == (0 if bool(valid_q.all()) else _native.DEV_BAD_LAST_INDEX)
+
+
+def test_mirror_from_lens_partial_and_negative_lengths():
+    n = 500
+    inp = small_inputs(n, 16)
+    q = torch.randn((3, 6, 256), dtype=torch.bfloat16)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    lens = torch.tensor([100, -7, 250], dtype=torch.int64)  # sum (negative as 0) = 350 < N
+    dev = inp.to(DEV)
+    qd = q.to(DEV)
+    welm.rope_mirror_from_lens(qd, dev.key, dev.positions, dev.cache, lens.to(DEV), status=status)
+    torch.cuda.synchronize()
+    assert status.item() == _native.DEV_BAD_LENGTH
+    k_got = dev.key.cpu()
+    assert_bitexact(k_got[:350], rope_oracle.apply_reference(inp.key[:350], inp.positions[:350], inp.cache), "key")
+    assert torch.equal(k_got[350:], inp.key[350:])
+    last = torch.tensor([99, 99, 349])
+    assert_bitexact(qd, rope_oracle.apply_reference(q, inp.positions[last], inp.cache), "query")

@@ -194,3 +194,17 @@ def test_static_host_entry_rejects_oversized_batches_before_any_cuda_call():
     assert lib.welm_rope_ordinary_host_static(None, FAKE, FAKE, FAKE, 4, 1536, 256, 16, None, None) == \
         _native.ERR_NULL_POINTER
     assert lib.welm_rope_ordinary_host_static(None, None, None, None, 0, 0, 0, 0, None, None) == _native.OK
+
+
+def test_mirror_from_lens_host_validation():
+    lib = _native.load()
+    args = lambda **kw: [kw.get(n, d) for n, d in (("q", FAKE), ("k", FAKE), ("p", FAKE), ("c", FAKE), ("l", FAKE),
+                                                   ("n", 16), ("bs", 2), ("qs", 1536), ("ks", 256), ("mp", 16),
+                                                   ("st", None), ("s", None))]
+    f = lib.welm_rope_mirror_from_lens
+    assert f(*args(bs=_native.LENS_MAX_BATCH + 1)) == _native.ERR_BAD_SIZE
+    assert f(*args(n=-1)) == _native.ERR_BAD_SIZE
+    assert f(*args(l=None)) == _native.ERR_NULL_POINTER
+    assert f(*args(l=FAKE + 4)) == _native.ERR_BAD_STRIDE  # lengths must be 8-byte aligned
+    assert f(*args(bs=2, qs=8)) == _native.ERR_BAD_STRIDE
+    assert f(*args(q=None, k=None, p=None, c=None, l=None, bs=0)) == _native.OK
