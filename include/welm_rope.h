@@ -59,6 +59,7 @@ typedef enum welm_rope_status {
 #define WELM_ROPE_DEV_BAD_LAST_INDEX 2 /* last_index[b] outside [0, N)                  */
 #define WELM_ROPE_DEV_BAD_TILE 4       /* tile start/end outside [0, N], or > 64 tokens */
 #define WELM_ROPE_DEV_BAD_LENGTH 8     /* negative request length (tile builder)        */
+#define WELM_ROPE_DEV_BAD_SLOT 16      /* slot_mapping[t] >= num_slots (KV-cache write) */
 
 /* Fixed model contract (bench_welmv4_inplace_rope_npu.py:48-58): head_dim 256, rope_dim 64, 6 Q heads,
  * 1 K head, 64-token work tiles. */
@@ -136,6 +137,38 @@ int welm_rope_mirror_from_lens(void* q, void* k, const int64_t* positions,
                                int64_t q_token_stride, int64_t k_token_stride,
                                int64_t max_position, int32_t* device_status,
                                void* stream);
+
+/*
+ * KV-mirror prefill fused with the paged KV-cache write and the Q last-row
+ * extraction, in one pass:
+ *   q_out[b]            = rope(q[last_index[b]]) at positions[last_index[b]]
+ *                         (all 6 heads, lanes 0..191 copied, 192..255 rotated)
+ *   key_cache[slot[t]]  = rope(k[t]) at positions[t]   (all 256 lanes)
+ *   value_cache[slot[t]] = v[t]                        (all 256 lanes)
+ * for t < N with slot[t] = slot_mapping[t]; slot < 0 marks a padding token
+ * and writes nothing, slot >= num_slots raises WELM_ROPE_DEV_BAD_SLOT and
+ * writes nothing; a token whose position is out of range is flagged and not
+ * written.  q, k and v are read only (q is the full [N, 6, 256] projection
+ * output; q_out holds BS rows); cache rows are `cache_slot_stride` elements
+ * apart (256 for [blocks, block_size, 1, 256] and [blocks, 1, block_size, 256]
+ * caches with one KV head).  value_cache / v may be NULL to skip the V copy.
+ * Every pointer must be 16-byte aligned and every stride a multiple of 8
+ * elements.
+ *
+ * Row 2 of the path's "next" list: the mirror's K output is what gets written
+ * to the KV cache (bench_welmv4_inplace_rope_npu.py:17-18 — only the last
+ * token per request keeps a Q row); the reference rotates in place and leaves
+ * the extraction and the cache write to separate passes.
+ */
+int welm_rope_mirror_kv_write(const void* q, void* q_out, const void* k, const void* v,
+                              const int64_t* positions, const float* cos_sin_cache,
+                              const int64_t* last_index, const int64_t* slot_mapping,
+                              void* key_cache, void* value_cache, int64_t n_tokens,
+                              int64_t batch_size, int64_t q_token_stride,
+                              int64_t q_out_token_stride, int64_t k_token_stride,
+                              int64_t v_token_stride, int64_t cache_slot_stride,
+                              int64_t num_slots, int64_t max_position,
+                              int32_t* device_status, void* stream);
 
 /*
  * Segmented 64-token tile-boundary builder on the device.  For request r of

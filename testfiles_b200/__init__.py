@@ -17,6 +17,7 @@ from .ops import (  # noqa: F401
     build_segment_tile_starts_device,
     count_segment_tiles,
     rope_mirror_from_lens,
+    rope_mirror_kv_write,
     rope_mirror_prefill,
     rope_prefill,
     segment_placeholder,

@@ -30,6 +30,7 @@ DEV_BAD_POSITION = 1
 DEV_BAD_LAST_INDEX = 2
 DEV_BAD_TILE = 4
 DEV_BAD_LENGTH = 8
+DEV_BAD_SLOT = 16
 
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
@@ -39,6 +40,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "welm_rope_ordinary": (ctypes.c_int, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P]),
     "welm_rope_mirror": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P]),
     "welm_rope_mirror_from_lens": (ctypes.c_int, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _P, _P]),
+    "welm_rope_mirror_kv_write": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64,
+                                                 _I64, _I64, _I64, _I64, _I64, _P, _P]),
     "welm_rope_build_tiles": (ctypes.c_int, [_P, _I64, _P, _I64, _P, _P, _P, _P]),
     "welm_rope_copy_rope_lanes": (ctypes.c_int, [_P, _P, _I64, _I64, _I64, _I64, _I64, _P]),
     "welm_rope_ordinary_host_static": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _P]),

@@ -50,6 +50,7 @@ __all__ = [
     "rope_prefill",
     "rope_mirror_prefill",
     "rope_mirror_from_lens",
+    "rope_mirror_kv_write",
     "build_segment_tile_starts",
     "build_segment_tile_starts_device",
     "count_segment_tiles",
@@ -233,6 +234,65 @@ def welmv4_inplace_rope_npu(
 
 
 welmv4_inplace_rope = welmv4_inplace_rope_npu
+
+
+def rope_mirror_kv_write(
+    q: torch.Tensor,
+    q_out: torch.Tensor,
+    k: torch.Tensor,
+    v: Optional[torch.Tensor],
+    positions: torch.Tensor,
+    cos_sin_cache: torch.Tensor,
+    last_index: torch.Tensor,
+    slot_mapping: torch.Tensor,
+    key_cache: torch.Tensor,
+    value_cache: Optional[torch.Tensor] = None,
+    status: Optional[torch.Tensor] = None,
+) -> None:
+    """KV-mirror prefill fused with the paged KV-cache write and the Q
+    last-row extraction (one pass, inputs read only):
+
+    * ``q_out[b] = rope(q[last_index[b]])`` — q is the full ``[N, 6, 256]``
+      projection output, q_out has one row per request;
+    * ``key_cache[slot] = rope(k[t])`` and ``value_cache[slot] = v[t]`` for
+      ``slot = slot_mapping[t] >= 0`` (negative slots are padding tokens).
+
+    Caches are contiguous bf16 tensors with one KV head of 256 lanes per slot,
+    e.g. ``[num_blocks, block_size, 1, 256]`` or ``[num_blocks, 1,
+    block_size, 256]`` (slot = block * block_size + offset in both).
+    """
+    device = _check_common(q, k, positions, cos_sin_cache)
+    _require(q_out, "q_out", torch.bfloat16, device)
+    _check_heads(q_out, "q_out", NUM_Q_HEADS)
+    _require(last_index, "last_index", torch.int64, device)
+    _require(slot_mapping, "slot_mapping", torch.int64, device)
+    _require(key_cache, "key_cache", torch.bfloat16, device)
+    if (v is None) != (value_cache is None):
+        raise ValueError("pass both v and value_cache, or neither")
+    if v is not None:
+        _require(v, "v", torch.bfloat16, device)
+        _check_heads(v, "v", NUM_K_HEADS)
+        _require(value_cache, "value_cache", torch.bfloat16, device)
+    for name, t in (("key_cache", key_cache), ("value_cache", value_cache)):
+        if t is not None and (not t.is_contiguous() or t.numel() % HEAD_DIM):
+            raise ValueError(f"{name} must be contiguous with {HEAD_DIM} lanes per slot")
+    if value_cache is not None and value_cache.numel() != key_cache.numel():
+        raise ValueError("key_cache and value_cache must hold the same number of slots")
+    for name, t in (("last_index", last_index), ("slot_mapping", slot_mapping)):
+        if t.dim() != 1 or (t.numel() > 1 and t.stride(0) != 1):
+            raise ValueError(f"{name} must be a contiguous 1-D int64 tensor")
+    n = int(positions.shape[0])
+    batch = int(last_index.numel())
+    if k.shape[0] != n or q.shape[0] < n or slot_mapping.numel() != n or (v is not None and v.shape[0] != n):
+        raise ValueError("q, k, v and slot_mapping need one row per token")
+    if q_out.shape[0] != batch:
+        raise ValueError("q_out needs one row per request (last_index entry)")
+    rc = _native.load().welm_rope_mirror_kv_write(
+        _ptr(q), _ptr(q_out), _ptr(k), _ptr(v), _ptr(positions), _ptr(cos_sin_cache), _ptr(last_index),
+        _ptr(slot_mapping), _ptr(key_cache), _ptr(value_cache), n, batch, int(q.stride(0)), int(q_out.stride(0)),
+        int(k.stride(0)), int(v.stride(0)) if v is not None else 0, HEAD_DIM, key_cache.numel() // HEAD_DIM,
+        int(cos_sin_cache.shape[0]), _status_ptr(status, device), _stream(device))
+    _native.check("welm_rope_mirror_kv_write", rc)
 
 
 def rope_mirror_from_lens(

@@ -208,3 +208,18 @@ def test_mirror_from_lens_host_validation():
     assert f(*args(l=FAKE + 4)) == _native.ERR_BAD_STRIDE  # lengths must be 8-byte aligned
     assert f(*args(bs=2, qs=8)) == _native.ERR_BAD_STRIDE
     assert f(*args(q=None, k=None, p=None, c=None, l=None, bs=0)) == _native.OK
+
+
+def test_kv_write_host_validation():
+    lib = _native.load()
+    base = dict(q=FAKE, qo=FAKE, k=FAKE, v=FAKE, p=FAKE, c=FAKE, li=FAKE, sl=FAKE, kc=FAKE, vc=FAKE, n=8, bs=2,
+                qs=1536, qos=1536, ks=256, vs=256, css=256, ns=64, mp=16)
+    order = ("q", "qo", "k", "v", "p", "c", "li", "sl", "kc", "vc", "n", "bs", "qs", "qos", "ks", "vs", "css", "ns", "mp")
+    f = lambda **kw: lib.welm_rope_mirror_kv_write(*[{**base, **kw}[x] for x in order], None, None)
+    assert f(n=-1) == _native.ERR_BAD_SIZE
+    assert f(sl=None) == _native.ERR_NULL_POINTER
+    assert f(v=None) == _native.ERR_NULL_POINTER  # v and value_cache come together
+    assert f(qo=None) == _native.ERR_NULL_POINTER
+    assert f(css=100) == _native.ERR_BAD_STRIDE
+    assert f(k=FAKE + 2) == _native.ERR_BAD_STRIDE  # 16-byte alignment required
+    assert f(q=None, qo=None, k=None, v=None, p=None, c=None, li=None, sl=None, kc=None, vc=None, n=0) == _native.OK
