@@ -88,6 +88,25 @@ __device__ __forceinline__ void pdl_enter() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// Work done BEFORE pdl_enter(), while the previous grid may still run: a
+// thread reads its position as a hint only (ld.global.cg: served from L2,
+// never allocated in L1, so no stale L1 line can answer the real loads made
+// after the wait) and prefetches that cos/sin row into L2.  A prefetch cannot
+// change a result — L2 is where writes of the previous grid land — and a
+// stale or garbage hint only fetches a useless line; hints outside the cache
+// are ignored.  The results use the positions read after the wait.
+__device__ __forceinline__ int64_t hint_load(const int64_t* p) {
+  int64_t v;
+  asm volatile("ld.global.cg.s64 %0, [%1];" : "=l"(v) : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ void prefetch_cos_sin_row(const float* cache, int64_t max_position, int64_t pos_hint,
+                                                     int part) {
+  if (part < 2 && pos_hint >= 0 && pos_hint < max_position)  // part 0: cos line, part 1: sin line
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(cache + pos_hint * kRopeDim + part * kHalf));
+}
+
 // ---------------------------------------------------------------------------
 // Loads / stores.  kVec: 16-byte vectors (bases 16-byte aligned, strides a
 // multiple of 8 elements); otherwise 2-byte scalars with the same results.
@@ -307,6 +326,12 @@ __device__ __forceinline__ void ordinary_token(const RopeArgs& a, int64_t tok, i
 template <bool kVec, Source kSrc>
 __global__ void __launch_bounds__(kBlock) rope_ordinary_kernel(const RopeArgs a) {
   extern __shared__ int32_t s_tab[];
+  if (kSrc != Source::kTileSlots) {  // tokens are items: warm the first item's cos/sin row
+    const int item0 = blockIdx.x * blockDim.x + threadIdx.x;
+    if (item0 < a.k_items)
+      prefetch_cos_sin_row(a.cache, a.max_position, hint_load(a.positions + (item0 >> kPartShift)),
+                           item0 & (kParts - 1));
+  }
   pdl_enter();
   if constexpr (kSrc == Source::kTileTable) {
     // One item per thread: tokens [0, k_items / 4), then one check per tile.
@@ -392,6 +417,18 @@ __device__ __forceinline__ void mirror_k_token(const RopeArgs& a, int64_t tok, i
 template <bool kVec, Source kSrc>
 __global__ void __launch_bounds__(kBlock) rope_mirror_kernel(const RopeArgs a) {
   extern __shared__ int32_t s_tab[];
+  {  // warm the first item's cos/sin row (Q rows: through a last_index hint)
+    const int item0 = blockIdx.x * blockDim.x + threadIdx.x;
+    const int part0 = item0 & (kParts - 1);
+    if (item0 < a.q_items) {
+      const int64_t src = hint_load(a.last_index + (item0 >> kPartShift));
+      if (src >= 0 && src < a.n_tokens)
+        prefetch_cos_sin_row(a.cache, a.max_position, hint_load(a.positions + src), part0);
+    } else if (kSrc != Source::kTileSlots && item0 - a.q_items < a.k_items) {
+      prefetch_cos_sin_row(a.cache, a.max_position, hint_load(a.positions + ((item0 - a.q_items) >> kPartShift)),
+                           part0);
+    }
+  }
   pdl_enter();
   if constexpr (kSrc == Source::kTileTable) {
     // One item per thread: Q rows, then tokens [0, k_items / 4), then one
@@ -494,6 +531,12 @@ __device__ __forceinline__ int64_t warp_request_ends(const int64_t* s, int n, in
 template <bool kVec>
 __global__ void __launch_bounds__(kBlock, 4) rope_mirror_lens_kernel(const RopeArgs a, const int64_t* lens, int batch) {
   extern __shared__ int64_t s_len[];
+  {  // K tokens: warm the first item's cos/sin row
+    const int item0 = blockIdx.x * blockDim.x + threadIdx.x;
+    if (item0 >= a.q_items && item0 - a.q_items < a.k_items)
+      prefetch_cos_sin_row(a.cache, a.max_position, hint_load(a.positions + ((item0 - a.q_items) >> kPartShift)),
+                           item0 & (kParts - 1));
+  }
   pdl_enter();
   for (int j = threadIdx.x; j < batch; j += blockDim.x) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(s_len + j)), "l"(lens + j) : "memory");
@@ -582,6 +625,18 @@ struct HeadPiece {
 };
 
 __global__ void __launch_bounds__(kBlock) rope_mirror_kv_write_kernel(const KvArgs a) {
+  {  // warm the first item's cos/sin row (Q rows: through a last_index hint)
+    const int item0 = blockIdx.x * blockDim.x + threadIdx.x;
+    const int part0 = item0 & (kParts - 1);
+    if (item0 < a.q_items) {
+      const int64_t src = hint_load(a.last_index + item0 / (kQHeads * kParts));
+      if (src >= 0 && src < a.n_tokens)
+        prefetch_cos_sin_row(a.cache, a.max_position, hint_load(a.positions + src), part0);
+    } else if (item0 - a.q_items < a.k_items) {
+      prefetch_cos_sin_row(a.cache, a.max_position, hint_load(a.positions + ((item0 - a.q_items) >> kPartShift)),
+                           part0);
+    }
+  }
   pdl_enter();
   const int stride = gridDim.x * blockDim.x;
   const int total = a.q_items + a.k_items;
