@@ -226,6 +226,61 @@ __device__ __forceinline__ bool gather_cos_sin(const RopeArgs& a, int64_t pos, i
   return true;
 }
 
+// Loads whose place in the instruction stream is pinned (volatile asm), so
+// they are issued where written — before the checks that decide whether
+// their values are used.
+__device__ __forceinline__ int64_t pinned_load_s64(const int64_t* p) {
+  int64_t v;
+  asm volatile("ld.global.nc.s64 %0, [%1];" : "=l"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float4 pinned_load_f4(const float* p) {
+  float4 v;
+  asm volatile("ld.global.nc.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+  return v;
+}
+
+// Cos/sin gather for a row whose position is known only at the end of a
+// dependent chain (position, or last_index -> position).  issue() starts, AFTER
+// the dependency wait, the loads that the chain would make if its values
+// equalled the hints read before the wait: positions[src_hint] and the cos/sin
+// row at pos_hint.  position() / finish() keep those values when the real src
+// and position equal the hints — the loads then read exactly the data the
+// chain would have read — and fall back to the real chain otherwise.  So the
+// common case costs one round trip instead of two or three, and every result
+// is the one the plain chain gives.  Hints < 0 disable the speculation.
+template <bool kVec>
+struct RowGather {
+  CosSin cs;
+  int64_t src_hint = -1, pos_hint = -1, pos_spec = 0;
+  bool src_spec = false, row_spec = false;
+  __device__ __forceinline__ void issue(const RopeArgs& a, int64_t sh, int64_t ph, int part) {
+    src_hint = sh;
+    pos_hint = ph;
+    src_spec = sh >= 0 && sh < a.n_tokens;
+    if (src_spec) pos_spec = pinned_load_s64(a.positions + sh);
+    row_spec = kVec && ph >= 0 && ph < a.max_position;
+    if (row_spec) {
+      const float* row = a.cache + ph * kRopeDim;
+      const float4 c0 = pinned_load_f4(row + part * kLanes), c1 = pinned_load_f4(row + part * kLanes + 4);
+      const float4 s0 = pinned_load_f4(row + kHalf + part * kLanes), s1 = pinned_load_f4(row + kHalf + part * kLanes + 4);
+      cs.c[0] = c0.x; cs.c[1] = c0.y; cs.c[2] = c0.z; cs.c[3] = c0.w;
+      cs.c[4] = c1.x; cs.c[5] = c1.y; cs.c[6] = c1.z; cs.c[7] = c1.w;
+      cs.s[0] = s0.x; cs.s[1] = s0.y; cs.s[2] = s0.z; cs.s[3] = s0.w;
+      cs.s[4] = s1.x; cs.s[5] = s1.y; cs.s[6] = s1.z; cs.s[7] = s1.w;
+    }
+  }
+  // Position of the row for the real src (already checked to be in [0, N)).
+  __device__ __forceinline__ int64_t position(const RopeArgs& a, int64_t src) const {
+    return src_spec && src == src_hint ? pos_spec : __ldg(a.positions + src);
+  }
+  // Cos/sin for the real position; false when it is outside the cache.
+  __device__ __forceinline__ bool finish(const RopeArgs& a, int64_t pos, int part) {
+    if (row_spec && pos == pos_hint) return true;
+    return gather_cos_sin<kVec>(a, pos, part, cs);
+  }
+};
+
 // ---------------------------------------------------------------------------
 // Token sources.  Tile semantics are the reference kernels'
 // (bench_welmv4_inplace_rope_npu.py:700-718, 856-867): tile i covers
@@ -308,29 +363,30 @@ __device__ __forceinline__ bool slot_token(const RopeArgs& a, int slot, int part
 // the cache row is gathered once for all seven heads.
 // ---------------------------------------------------------------------------
 template <bool kVec>
-__device__ __forceinline__ void ordinary_token(const RopeArgs& a, int64_t tok, int part) {
+__device__ __forceinline__ void ordinary_token(const RopeArgs& a, int64_t tok, int part, int64_t pos_hint) {
   const int64_t pos = __ldg(a.positions + tok);
   Slices<kVec, 1> kx;
   Slices<kVec, kQHeads> qx;
   kx.load(a.k + tok * a.k_stride, part);
   qx.load(a.q + tok * a.q_stride, part);
-  CosSin cs;
-  if (!gather_cos_sin<kVec>(a, pos, part, cs)) {
+  RowGather<kVec> g;
+  g.issue(a, -1, pos_hint, part);
+  if (!g.finish(a, pos, part)) {
     if (part == 0) raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
     return;
   }
-  kx.rotate_store(cs);
-  qx.rotate_store(cs);
+  kx.rotate_store(g.cs);
+  qx.rotate_store(g.cs);
 }
 
 template <bool kVec, Source kSrc>
 __global__ void __launch_bounds__(kBlock) rope_ordinary_kernel(const RopeArgs a) {
   extern __shared__ int32_t s_tab[];
-  if (kSrc != Source::kTileSlots) {  // tokens are items: warm the first item's cos/sin row
-    const int item0 = blockIdx.x * blockDim.x + threadIdx.x;
-    if (item0 < a.k_items)
-      prefetch_cos_sin_row(a.cache, a.max_position, hint_load(a.positions + (item0 >> kPartShift)),
-                           item0 & (kParts - 1));
+  const int item0 = blockIdx.x * blockDim.x + threadIdx.x;
+  int64_t pos_hint = -1;
+  if (kSrc != Source::kTileSlots && item0 < a.k_items) {  // tokens are items: warm the first item's row
+    pos_hint = hint_load(a.positions + (item0 >> kPartShift));
+    prefetch_cos_sin_row(a.cache, a.max_position, pos_hint, item0 & (kParts - 1));
   }
   pdl_enter();
   if constexpr (kSrc == Source::kTileTable) {
@@ -342,21 +398,22 @@ __global__ void __launch_bounds__(kBlock) rope_ordinary_kernel(const RopeArgs a)
     const int64_t tok = is_token ? (item >> kPartShift) : 0;
     Slices<kVec, 1> kx;
     Slices<kVec, kQHeads> qx;
-    CosSin cs;
+    RowGather<kVec> g;
     bool pos_ok = false;
     if (is_token) {
       const int64_t pos = __ldg(a.positions + tok);
       kx.load(a.k + tok * a.k_stride, part);
       qx.load(a.q + tok * a.q_stride, part);
-      pos_ok = gather_cos_sin<kVec>(a, pos, part, cs);
+      g.issue(a, -1, pos_hint, part);
+      pos_ok = g.finish(a, pos, part);
     } else if (item - a.k_items < a.num_tiles) {
       check_tile(a, item - a.k_items);
     }
     stage_table_wait();  // every thread of the CTA reaches this once
     if (is_token && table_covers(s_tab, a.num_tiles, tok)) {
       if (pos_ok) {
-        kx.rotate_store(cs);
-        qx.rotate_store(cs);
+        kx.rotate_store(g.cs);
+        qx.rotate_store(g.cs);
       } else if (part == 0) {
         raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
       }
@@ -366,7 +423,8 @@ __global__ void __launch_bounds__(kBlock) rope_ordinary_kernel(const RopeArgs a)
     for (int item = blockIdx.x * blockDim.x + threadIdx.x; item < a.k_items; item += stride) {
       const int part = item & (kParts - 1);
       int64_t tok;
-      if (slot_token<kSrc>(a, item >> kPartShift, part, tok)) ordinary_token<kVec>(a, tok, part);
+      if (slot_token<kSrc>(a, item >> kPartShift, part, tok))
+        ordinary_token<kVec>(a, tok, part, item == item0 ? pos_hint : -1);
     }
   }
 }
@@ -379,56 +437,60 @@ __global__ void __launch_bounds__(kBlock) rope_ordinary_kernel(const RopeArgs a)
 // tensors, so the two phases need no ordering.  A Q row's data loads are
 // issued before its last_index -> position -> cache chain.
 // ---------------------------------------------------------------------------
+// g has been issued (with or without hints) before src is known.
 template <bool kVec>
 __device__ __forceinline__ void finish_q_row(const RopeArgs& a, Slices<kVec, kQHeads>& qx, int64_t src,
-                                             int part) {
+                                             RowGather<kVec>& g, int part) {
   if (src < 0 || src >= a.n_tokens) {
     if (part == 0) raise_status(a.status, WELM_ROPE_DEV_BAD_LAST_INDEX);
     return;
   }
-  CosSin cs;
-  if (!gather_cos_sin<kVec>(a, __ldg(a.positions + src), part, cs)) {
+  if (!g.finish(a, g.position(a, src), part)) {
     if (part == 0) raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
     return;
   }
-  qx.rotate_store(cs);
+  qx.rotate_store(g.cs);
 }
 
 template <bool kVec>
-__device__ __forceinline__ void mirror_q_row(const RopeArgs& a, int b, int part) {
+__device__ __forceinline__ void mirror_q_row(const RopeArgs& a, int b, int part, int64_t src_hint,
+                                             int64_t pos_hint) {
   Slices<kVec, kQHeads> qx;
   qx.load(a.q + int64_t(b) * a.q_stride, part);
-  finish_q_row<kVec>(a, qx, __ldg(a.last_index + b), part);
+  const int64_t src = __ldg(a.last_index + b);
+  RowGather<kVec> g;
+  g.issue(a, src_hint, pos_hint, part);
+  finish_q_row<kVec>(a, qx, src, g, part);
 }
 
 template <bool kVec>
-__device__ __forceinline__ void mirror_k_token(const RopeArgs& a, int64_t tok, int part) {
+__device__ __forceinline__ void mirror_k_token(const RopeArgs& a, int64_t tok, int part, int64_t pos_hint) {
   const int64_t pos = __ldg(a.positions + tok);
   Slices<kVec, 1> kx;
   kx.load(a.k + tok * a.k_stride, part);
-  CosSin cs;
-  if (!gather_cos_sin<kVec>(a, pos, part, cs)) {
+  RowGather<kVec> g;
+  g.issue(a, -1, pos_hint, part);
+  if (!g.finish(a, pos, part)) {
     if (part == 0) raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
     return;
   }
-  kx.rotate_store(cs);
+  kx.rotate_store(g.cs);
 }
 
+// At most 128 registers: 4 CTAs per SM keep a 16384-token launch in one wave.
 template <bool kVec, Source kSrc>
-__global__ void __launch_bounds__(kBlock) rope_mirror_kernel(const RopeArgs a) {
+__global__ void __launch_bounds__(kBlock, 4) rope_mirror_kernel(const RopeArgs a) {
   extern __shared__ int32_t s_tab[];
-  {  // warm the first item's cos/sin row (Q rows: through a last_index hint)
-    const int item0 = blockIdx.x * blockDim.x + threadIdx.x;
-    const int part0 = item0 & (kParts - 1);
-    if (item0 < a.q_items) {
-      const int64_t src = hint_load(a.last_index + (item0 >> kPartShift));
-      if (src >= 0 && src < a.n_tokens)
-        prefetch_cos_sin_row(a.cache, a.max_position, hint_load(a.positions + src), part0);
-    } else if (kSrc != Source::kTileSlots && item0 - a.q_items < a.k_items) {
-      prefetch_cos_sin_row(a.cache, a.max_position, hint_load(a.positions + ((item0 - a.q_items) >> kPartShift)),
-                           part0);
-    }
+  // warm the first item's cos/sin row (Q rows: through a last_index hint)
+  const int item0 = blockIdx.x * blockDim.x + threadIdx.x;
+  int64_t src_hint = -1, pos_hint = -1;
+  if (item0 < a.q_items) {
+    src_hint = hint_load(a.last_index + (item0 >> kPartShift));
+    if (src_hint >= 0 && src_hint < a.n_tokens) pos_hint = hint_load(a.positions + src_hint);
+  } else if (kSrc != Source::kTileSlots && item0 - a.q_items < a.k_items) {
+    pos_hint = hint_load(a.positions + ((item0 - a.q_items) >> kPartShift));
   }
+  prefetch_cos_sin_row(a.cache, a.max_position, pos_hint, item0 & (kParts - 1));
   pdl_enter();
   if constexpr (kSrc == Source::kTileTable) {
     // One item per thread: Q rows, then tokens [0, k_items / 4), then one
@@ -444,25 +506,27 @@ __global__ void __launch_bounds__(kBlock) rope_mirror_kernel(const RopeArgs a) {
     const int64_t tok = is_token ? (k_item >> kPartShift) : 0;
     Slices<kVec, kQHeads> qx;
     Slices<kVec, 1> kx;
-    CosSin cs;
+    RowGather<kVec> g;
     bool pos_ok = false;
     int64_t src = 0;
     if (is_q) {
       qx.load(a.q + int64_t(item >> kPartShift) * a.q_stride, part);
       src = __ldg(a.last_index + (item >> kPartShift));
+      g.issue(a, src_hint, pos_hint, part);
     } else if (is_token) {
       const int64_t pos = __ldg(a.positions + tok);
       kx.load(a.k + tok * a.k_stride, part);
-      pos_ok = gather_cos_sin<kVec>(a, pos, part, cs);
+      g.issue(a, -1, pos_hint, part);
+      pos_ok = g.finish(a, pos, part);
     } else if (k_item - a.k_items < a.num_tiles) {
       check_tile(a, k_item - a.k_items);
     }
     stage_table_wait();
     if (is_q) {
-      finish_q_row<kVec>(a, qx, src, part);
+      finish_q_row<kVec>(a, qx, src, g, part);
     } else if (is_token && table_covers(s_tab, a.num_tiles, tok)) {
       if (pos_ok) {
-        kx.rotate_store(cs);
+        kx.rotate_store(g.cs);
       } else if (part == 0) {
         raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
       }
@@ -472,11 +536,13 @@ __global__ void __launch_bounds__(kBlock) rope_mirror_kernel(const RopeArgs a) {
     const int total = a.q_items + a.k_items;
     for (int item = blockIdx.x * blockDim.x + threadIdx.x; item < total; item += stride) {
       const int part = item & (kParts - 1);
+      const bool first = item == item0;
       if (item < a.q_items) {
-        mirror_q_row<kVec>(a, item >> kPartShift, part);
+        mirror_q_row<kVec>(a, item >> kPartShift, part, first ? src_hint : -1, first ? pos_hint : -1);
       } else {
         int64_t tok;
-        if (slot_token<kSrc>(a, (item - a.q_items) >> kPartShift, part, tok)) mirror_k_token<kVec>(a, tok, part);
+        if (slot_token<kSrc>(a, (item - a.q_items) >> kPartShift, part, tok))
+          mirror_k_token<kVec>(a, tok, part, first ? pos_hint : -1);
       }
     }
   }
@@ -531,11 +597,14 @@ __device__ __forceinline__ int64_t warp_request_ends(const int64_t* s, int n, in
 template <bool kVec>
 __global__ void __launch_bounds__(kBlock, 4) rope_mirror_lens_kernel(const RopeArgs a, const int64_t* lens, int batch) {
   extern __shared__ int64_t s_len[];
-  {  // K tokens: warm the first item's cos/sin row
+  // K tokens: warm the first item's cos/sin row
+  int64_t pos_hint = -1;
+  {
     const int item0 = blockIdx.x * blockDim.x + threadIdx.x;
-    if (item0 >= a.q_items && item0 - a.q_items < a.k_items)
-      prefetch_cos_sin_row(a.cache, a.max_position, hint_load(a.positions + ((item0 - a.q_items) >> kPartShift)),
-                           item0 & (kParts - 1));
+    if (item0 >= a.q_items && item0 - a.q_items < a.k_items) {
+      pos_hint = hint_load(a.positions + ((item0 - a.q_items) >> kPartShift));
+      prefetch_cos_sin_row(a.cache, a.max_position, pos_hint, item0 & (kParts - 1));
+    }
   }
   pdl_enter();
   for (int j = threadIdx.x; j < batch; j += blockDim.x) {
@@ -550,14 +619,15 @@ __global__ void __launch_bounds__(kBlock, 4) rope_mirror_lens_kernel(const RopeA
   const int64_t tok = is_token ? (k_item >> kPartShift) : 0;
   Slices<kVec, kQHeads> qx;
   Slices<kVec, 1> kx;
-  CosSin cs;
+  RowGather<kVec> g;
   bool pos_ok = false;
   if (is_q) {
     qx.load(a.q + int64_t(item >> kPartShift) * a.q_stride, part);
   } else if (is_token) {
     const int64_t pos = __ldg(a.positions + tok);
     kx.load(a.k + tok * a.k_stride, part);
-    pos_ok = gather_cos_sin<kVec>(a, pos, part, cs);
+    g.issue(a, -1, pos_hint, part);
+    pos_ok = g.finish(a, pos, part);
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
@@ -565,10 +635,10 @@ __global__ void __launch_bounds__(kBlock, 4) rope_mirror_lens_kernel(const RopeA
   bool negative = false;
   const int64_t total = warp_request_ends(s_len, batch, is_q ? (item >> kPartShift) : -1, end_row, negative);
   if (is_q) {
-    finish_q_row<kVec>(a, qx, end_row - 1, part);
+    finish_q_row<kVec>(a, qx, end_row - 1, g, part);  // g was not issued: plain chain
   } else if (is_token && tok < total) {
     if (pos_ok) {
-      kx.rotate_store(cs);
+      kx.rotate_store(g.cs);
     } else if (part == 0) {
       raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
     }
