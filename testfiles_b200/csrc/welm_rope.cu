@@ -101,6 +101,14 @@ __device__ __forceinline__ int64_t hint_load(const int64_t* p) {
   return v;
 }
 
+// Prefetches the 128-byte lines of [p, p + bytes) into L2 (one line per thread
+// of the CTA; every CTA stages the whole table, so every CTA asks for it).
+__device__ __forceinline__ void prefetch_lines(const void* p, int64_t bytes) {
+  const char* base = static_cast<const char*>(p);
+  for (int64_t off = int64_t(threadIdx.x) * 128; off < bytes; off += int64_t(blockDim.x) * 128)
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(base + off));
+}
+
 __device__ __forceinline__ void prefetch_cos_sin_row(const float* cache, int64_t max_position, int64_t pos_hint,
                                                      int part) {
   if (part < 2 && pos_hint >= 0 && pos_hint < max_position)  // part 0: cos line, part 1: sin line
@@ -384,6 +392,7 @@ __global__ void __launch_bounds__(kBlock) rope_ordinary_kernel(const RopeArgs a)
   extern __shared__ int32_t s_tab[];
   const int item0 = blockIdx.x * blockDim.x + threadIdx.x;
   int64_t pos_hint = -1;
+  if (kSrc == Source::kTileTable) prefetch_lines(a.tile_starts, int64_t(a.num_tiles + 1) * sizeof(int32_t));
   if (kSrc != Source::kTileSlots && item0 < a.k_items) {  // tokens are items: warm the first item's row
     pos_hint = hint_load(a.positions + (item0 >> kPartShift));
     prefetch_cos_sin_row(a.cache, a.max_position, pos_hint, item0 & (kParts - 1));
@@ -484,6 +493,7 @@ __global__ void __launch_bounds__(kBlock, 4) rope_mirror_kernel(const RopeArgs a
   // warm the first item's cos/sin row (Q rows: through a last_index hint)
   const int item0 = blockIdx.x * blockDim.x + threadIdx.x;
   int64_t src_hint = -1, pos_hint = -1;
+  if (kSrc == Source::kTileTable) prefetch_lines(a.tile_starts, int64_t(a.num_tiles + 1) * sizeof(int32_t));
   if (item0 < a.q_items) {
     src_hint = hint_load(a.last_index + (item0 >> kPartShift));
     if (src_hint >= 0 && src_hint < a.n_tokens) pos_hint = hint_load(a.positions + src_hint);
@@ -597,8 +607,9 @@ __device__ __forceinline__ int64_t warp_request_ends(const int64_t* s, int n, in
 template <bool kVec>
 __global__ void __launch_bounds__(kBlock, 4) rope_mirror_lens_kernel(const RopeArgs a, const int64_t* lens, int batch) {
   extern __shared__ int64_t s_len[];
-  // K tokens: warm the first item's cos/sin row
+  // K tokens: warm the first item's cos/sin row; the lengths every CTA stages
   int64_t pos_hint = -1;
+  prefetch_lines(lens, int64_t(batch) * sizeof(int64_t));
   {
     const int item0 = blockIdx.x * blockDim.x + threadIdx.x;
     if (item0 >= a.q_items && item0 - a.q_items < a.k_items) {

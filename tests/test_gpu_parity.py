@@ -464,3 +464,31 @@ def test_mirror_from_lens_partial_and_negative_lengths():
     assert torch.equal(k_got[350:], inp.key[350:])
     last = torch.tensor([99, 99, 349])
     assert_bitexact(qd, rope_oracle.apply_reference(q, inp.positions[last], inp.cache), "query")
+
+
+def test_launches_without_programmatic_dependent_launch():
+    """WELM_ROPE_PDL=0 launches plainly (no early scheduling); results are the
+    same bits.  The switch is read once per process, so a child runs it."""
+    import subprocess
+    import sys
+    import textwrap
+
+    from conftest import REPO
+
+    code = textwrap.dedent("""
+        import torch, testfiles_b200 as welm
+        from oracle import rope_oracle
+        from testfiles_b200 import workloads
+        for name in ("b_prefill_m577", "b_mirror_segmented_n8192_bs16_uneven", "b_decode_m3"):
+            inp = workloads.make_inputs(workloads.find_case(name), "cpu")
+            d = inp.to("cuda:0")
+            welm.welmv4_inplace_rope_npu(d.query, d.key, d.positions, d.cache, d.last_index, d.segment_tile_starts)
+            torch.cuda.synchronize()
+            q, k = rope_oracle.reference_outputs(inp.query, inp.key, inp.positions, inp.last_index, inp.cache)
+            assert torch.equal(d.query.cpu().view(torch.int16), q.view(torch.int16)), name
+            assert torch.equal(d.key.cpu().view(torch.int16), k.view(torch.int16)), name
+        print("ok")
+    """)
+    env = dict(__import__("os").environ, WELM_ROPE_PDL="0")
+    out = subprocess.run([sys.executable, "-c", code], cwd=REPO, env=env, capture_output=True, text=True, timeout=240)
+    assert out.returncode == 0 and out.stdout.strip().endswith("ok"), out.stderr[-2000:]
