@@ -11,6 +11,12 @@ checking (:func:`gather_rows`).
   balanced by token count (:func:`shard_requests`); each rank gets its K rows,
   its Q rows, ``last_index`` rebased to its local token offset and a locally
   rebuilt ``segment_tile_starts`` (:func:`local_batch`).
+
+Failures stay on the host: each rank folds its C-ABI return code and device
+status word into one integer, and :func:`agree_status` (a MAX all-reduce,
+the step before any gather) tells every rank whether any rank failed, so all
+ranks take the same next collective or none.  A rank that died outright
+surfaces as an error of that collective within the process group's timeout.
 """
 
 from __future__ import annotations
@@ -135,3 +141,36 @@ def gather_rows(local: torch.Tensor, counts: Sequence[int], group=None) -> Optio
     if rank != 0:
         return None
     return torch.cat([p[: int(c)] for p, c in zip(parts, counts)], dim=0)
+
+
+class RankFailure(RuntimeError):
+    """Raised on every rank when any rank reported a non-zero status."""
+
+    def __init__(self, status: int):
+        super().__init__(f"a rank reported status {status:#x}; the gather was skipped on every rank")
+        self.status = status
+
+
+def agree_status(status: int, group=None, device: Optional[torch.device] = None) -> int:
+    """MAX of every rank's status; every rank gets the same answer.
+
+    ``status`` is 0 for success.  Fold a C-ABI return code ``rc`` and a device
+    status word ``dev`` as ``rc << 8 | dev`` so either one makes it non-zero.
+    NCCL groups need ``device`` (the rank's CUDA device); gloo runs on CPU.
+    """
+    import torch.distributed as dist
+
+    if status < 0:
+        raise ValueError("status must be non-negative")
+    if device is None:
+        device = torch.device("cpu")
+    t = torch.tensor([int(status)], dtype=torch.int64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    return int(t.item())
+
+
+def check_all_ranks(status: int, group=None, device: Optional[torch.device] = None) -> None:
+    """:func:`agree_status`, raising :class:`RankFailure` on every rank if any failed."""
+    agreed = agree_status(status, group, device)
+    if agreed:
+        raise RankFailure(agreed)

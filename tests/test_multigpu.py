@@ -47,7 +47,10 @@ def _worker(rank: int, world: int, port: int, queue) -> None:
         pos = full.positions[t0:t1].to(dev)
         last = torch.tensor(local.last_index, dtype=torch.int64, device=dev)
         starts = torch.tensor(local.tile_starts, dtype=torch.int32, device=dev)
-        welm.welmv4_inplace_rope_npu(q, k, pos, full.cache.to(dev), last, starts)
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        welm.welmv4_inplace_rope_npu(q, k, pos, full.cache.to(dev), last, starts, status=status)
+        # every rank learns of any rank's device status before the gather
+        sharding.check_all_ranks(int(status.item()), device=dev)
         k_counts = [sharding.local_batch(lens, rr).n_tokens for rr in ranges]
         q_counts = [rr[1] - rr[0] for rr in ranges]
         k_all = sharding.gather_rows(k, k_counts)

@@ -4,7 +4,9 @@ The fixtures in tests/golden were produced by the reference's own
 ``make_cos_sin_cache`` / ``make_inputs`` / ``reference_outputs``
 (bench_welmv4_inplace_rope_npu.py:1391-1521) by tests/golden/gen_golden.py.
 Here the restated oracle must reproduce every output digest bit for bit,
-and ``testfiles_b200.workloads`` must reproduce every input digest.
+and ``testfiles_b200.workloads`` must reproduce every input digest.  The
+plain-C restatement (oracle/rope_oracle.c, through oracle/c_oracle.py) is held
+to the same digests and to the reference's tile tables.
 """
 
 from __future__ import annotations
@@ -13,7 +15,7 @@ import pytest
 import torch
 
 from conftest import digest
-from oracle import rope_oracle
+from oracle import c_oracle, rope_oracle
 from testfiles_b200 import workloads
 
 CASES = {c.name: c for c in workloads.reference_cases() + workloads.baseline_cases()}
@@ -52,6 +54,9 @@ def test_oracle_reproduces_reference(name, golden_outputs):
     q_out, k_out = rope_oracle.reference_outputs(inp.query, inp.key, inp.positions, inp.last_index, inp.cache)
     assert digest(q_out) == rec["outputs"]["query"]
     assert digest(k_out) == rec["outputs"]["key"]
+    q_c, k_c = c_oracle.reference_outputs(inp.query, inp.key, inp.positions, inp.last_index, inp.cache)
+    assert digest(q_c) == rec["outputs"]["query"], "C oracle differs from the reference"
+    assert digest(k_c) == rec["outputs"]["key"], "C oracle differs from the reference"
 
 
 def test_oracle_tile_builder_matches_reference_tables(tile_tables):
@@ -62,6 +67,7 @@ def test_oracle_tile_builder_matches_reference_tables(tile_tables):
         if rec["last_index"] is not None:
             assert rope_oracle.make_last_index(sum(lens), len(lens), lens) == rec["last_index"], name
         assert workloads.tile_starts_for(tuple(lens)) == rec["segment_tile_starts"], name
+        assert c_oracle.build_tiles(lens) == rec["segment_tile_starts"], name
 
 
 def test_oracle_uneven_lengths():
@@ -95,3 +101,35 @@ def test_position_zero_is_identity():
     x = torch.randn(5, 6, 256, dtype=torch.bfloat16)
     out = rope_oracle.apply_reference(x, torch.zeros(5, dtype=torch.int64), cache)
     assert torch.equal(out, x)
+
+
+def test_c_oracle_matches_torch_oracle_on_edge_values():
+    """NaN / Inf / subnormal / out-of-range positions: the C restatement and
+    the torch restatement agree bit for bit (bad rows are left unrotated)."""
+    g = torch.Generator().manual_seed(7)
+    cache = rope_oracle.make_cos_sin_cache(64, 10000.0)
+    x = torch.randn(40, 3, 256, generator=g).to(torch.bfloat16)
+    bits = x.view(torch.int16)
+    bits[0, 0, 192:200] = torch.tensor([0x7FC0, 0x7F80, -128, 0x0001, -32767, 0x7F7F, -129, 0x7F81], dtype=torch.int16)
+    bits[1, 2, 224:256] = 0x0001  # subnormal x2
+    pos = torch.randint(0, 64, (40,), generator=g)
+    pos[5] = 63
+    out_t = rope_oracle.apply_reference(x, pos, cache)
+    out_c = c_oracle.apply(x, pos, cache)
+    # a rotated NaN's payload is not pinned (torch's vectorised CPU conversion
+    # writes 0xFFFF, its scalar one 0x7FC0): NaN must meet NaN, the rest bits
+    nan = torch.isnan(out_t)
+    assert nan.any() and torch.equal(nan, torch.isnan(out_c))
+    assert torch.equal(out_t.view(torch.int16)[~nan], out_c.view(torch.int16)[~nan])
+    bad = pos.clone()
+    bad[3], bad[4] = -1, 64
+    out_b = c_oracle.apply(x, bad, cache)
+    keep = torch.ones(40, dtype=torch.bool)
+    keep[3:5] = False
+    assert torch.equal(out_b[keep].view(torch.int16), out_c[keep].view(torch.int16))
+    assert torch.equal(out_b[3:5].view(torch.int16), x[3:5].view(torch.int16))
+
+
+def test_c_oracle_tile_builder_edge_lengths():
+    for lens in ([], [0], [0, 0, 5], [64], [65, 0, 128, 1], [1] * 70, [4096, 3]):
+        assert c_oracle.build_tiles(lens) == rope_oracle.build_tile_starts(lens), lens
