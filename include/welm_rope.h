@@ -18,7 +18,8 @@
  * device status word and the stream.
  *
  * Conventions for every entry point:
- *   - pointers are device pointers (except the *_host functions);
+ *   - pointers are device pointers (except the *_host functions and
+ *     welm_rope_ordinary_mapped);
  *   - token strides are in ELEMENTS (torch `tensor.stride(0)`); the six Q
  *     heads of a token are contiguous (head stride 256 elements);
  *   - `stream` is a cudaStream_t / CUstream handle (NULL = legacy default
@@ -51,7 +52,8 @@ typedef enum welm_rope_status {
   WELM_ROPE_ERR_BAD_STRIDE = 4,   /* token stride makes rows overlap              */
   WELM_ROPE_ERR_CAPACITY = 5,     /* output buffer too small (tile builder)       */
   WELM_ROPE_ERR_CUDA = 6,         /* the CUDA runtime refused the launch          */
-  WELM_ROPE_ERR_TOO_MANY_TOKENS = 7 /* more tokens than the static staging area holds */
+  WELM_ROPE_ERR_TOO_MANY_TOKENS = 7, /* more tokens than the static staging area holds */
+  WELM_ROPE_ERR_NOT_MAPPED = 8       /* a host buffer is not page-locked and mapped for the device */
 } welm_rope_status;
 
 /* Device-side status bits (ORed into *device_status when it is non-NULL). */
@@ -250,6 +252,34 @@ int welm_rope_ordinary_host_static(void* q, void* k, const int64_t* positions,
                                    int64_t q_token_stride, int64_t k_token_stride,
                                    int64_t max_position, int32_t* device_status,
                                    void* stream);
+
+/*
+ * Ordinary prefill / decode RoPE on Q [n_tokens, 6, 256] and K [n_tokens, 1,
+ * 256] that stay in page-locked host memory, without staging: one kernel reads
+ * each 128-byte rope slice (lanes 192..255 of a head) straight from host
+ * memory over PCIe, rotates it and writes it back, so the two bus directions
+ * overlap and lanes 0..191 never cross the bus.  q and k must be page-locked
+ * AND mapped into the device's address space (cudaHostAlloc / cudaMallocHost,
+ * torch's pin_memory(), or cudaHostRegister with cudaHostRegisterMapped), each
+ * within one allocation; positions may be such host memory or device memory
+ * of the current device; cos_sin_cache is device memory.  Other memory is
+ * rejected with WELM_ROPE_ERR_NOT_MAPPED before anything is launched.  Bases
+ * must be 16-byte aligned and token strides multiples of 8 elements
+ * (WELM_ROPE_ERR_BAD_STRIDE otherwise).
+ *
+ * Stream-ordered like the device entries: the host buffers hold the result
+ * once `stream` has been synchronised, and the host must not touch them in
+ * between.  Allocates nothing; out-of-range positions leave their token
+ * unchanged and raise WELM_ROPE_DEV_BAD_POSITION.
+ *
+ * No counterpart in the reference (its Q and K always live on the device); it
+ * serves callers that keep Q/K in host memory.
+ */
+int welm_rope_ordinary_mapped(void* q, void* k, const int64_t* positions,
+                              const float* cos_sin_cache, int64_t n_tokens,
+                              int64_t q_token_stride, int64_t k_token_stride,
+                              int64_t max_position, int32_t* device_status,
+                              void* stream);
 
 /* Human-readable name of a welm_rope_status code (static storage). */
 const char* welm_rope_status_string(int status);

@@ -22,6 +22,7 @@ ERR_BAD_STRIDE = 4
 ERR_CAPACITY = 5
 ERR_CUDA = 6
 ERR_TOO_MANY_TOKENS = 7
+ERR_NOT_MAPPED = 8
 STATIC_MAX_TOKENS = 2048
 LENS_MAX_BATCH = 2048
 
@@ -45,6 +46,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "welm_rope_build_tiles": (ctypes.c_int, [_P, _I64, _P, _I64, _P, _P, _P, _P]),
     "welm_rope_copy_rope_lanes": (ctypes.c_int, [_P, _P, _I64, _I64, _I64, _I64, _I64, _P]),
     "welm_rope_ordinary_host_static": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _P]),
+    "welm_rope_ordinary_mapped": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _P]),
     "welm_rope_count_tiles_host": (ctypes.c_int, [_P, _I64, _P]),
     "welm_rope_build_tiles_host": (ctypes.c_int, [_P, _I64, _P, _I64, _P, _P]),
     "welm_rope_status_string": (ctypes.c_char_p, [ctypes.c_int]),

@@ -923,6 +923,78 @@ rope_staged_kernel(uint16_t* q, uint16_t* k, const int64_t* positions, const flo
 }
 
 // ---------------------------------------------------------------------------
+// Mapped-host entry (welm_rope_ordinary_mapped): Q and K stay in page-locked
+// host memory mapped into the device's address space, and the kernel moves
+// only the rope slices over PCIe, reading and writing in the same pass so the
+// two bus directions overlap.  One piece = the 128-byte rope slice (64 lanes)
+// of one head of one token; pieces are numbered token-major (6 Q heads, then
+// K).  Eight consecutive threads own a piece, 16 bytes each, so every warp
+// request covers whole 128-byte slices — the request size at which the
+// bus's reads and writes run near their bulk-copy rate.  Thread sub =
+// lane & 7 holds x1 lanes 8*sub.. (sub < 4) or the matching x2 lanes
+// (sub >= 4); the other half of its pair arrives by shuffle, both threads
+// rotate the pair with the same rotate8 and each stores its own half.
+// ---------------------------------------------------------------------------
+constexpr int kMappedBlock = 256;
+constexpr int kMappedPieces = kQHeads + 1;  // pieces per token
+constexpr int kPieceThreads = 8;            // 16-byte vectors per piece
+
+struct MappedArgs {
+  uint16_t* q;
+  uint16_t* k;
+  const int64_t* positions;
+  const float* cache;
+  int64_t q_stride;
+  int64_t k_stride;
+  int64_t max_position;
+  int64_t pieces;   // n_tokens * kMappedPieces
+  int64_t threads;  // pieces * kPieceThreads rounded up to whole warps
+  int32_t* status;
+};
+
+__global__ void __launch_bounds__(kMappedBlock) rope_mapped_kernel(const MappedArgs a) {
+  pdl_enter();
+  const int sub = threadIdx.x & (kPieceThreads - 1);
+  const int part = sub & (kParts - 1);
+  const bool upper = sub >= kParts;
+  const int64_t stride = int64_t(gridDim.x) * blockDim.x;
+  // a.threads is a multiple of 32 and so is the stride: every lane of a warp
+  // runs the same iterations, which the shuffles below need.
+  for (int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; t < a.threads; t += stride) {
+    const int64_t piece = t / kPieceThreads;
+    const bool valid = piece < a.pieces;
+    int64_t tok = 0, pos = 0;
+    int j = 0;
+    uint16_t* addr = nullptr;
+    uint4 mine = make_uint4(0u, 0u, 0u, 0u);
+    if (valid) {
+      tok = piece / kMappedPieces;
+      j = int(piece - tok * kMappedPieces);
+      uint16_t* row = j < kQHeads ? a.q + tok * a.q_stride + j * kHeadDim : a.k + tok * a.k_stride;
+      addr = row + kRopeLane0 + (upper ? kHalf : 0) + part * kLanes;
+      mine = *reinterpret_cast<const uint4*>(addr);
+      pos = a.positions[tok];
+    }
+    uint4 other;
+    other.x = __shfl_xor_sync(0xffffffffu, mine.x, kParts);
+    other.y = __shfl_xor_sync(0xffffffffu, mine.y, kParts);
+    other.z = __shfl_xor_sync(0xffffffffu, mine.z, kParts);
+    other.w = __shfl_xor_sync(0xffffffffu, mine.w, kParts);
+    if (!valid) continue;
+    if (pos < 0 || pos >= a.max_position) {
+      if (sub == 0 && j == kQHeads) raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
+      continue;  // the token stays as it was
+    }
+    CosSin cs;
+    Io<true>::load_cos_sin(a.cache + pos * kRopeDim, part, cs);
+    uint4 x1 = upper ? other : mine;
+    uint4 x2 = upper ? mine : other;
+    rotate8(x1, x2, cs);
+    *reinterpret_cast<uint4*>(addr) = upper ? x2 : x1;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side.
 // ---------------------------------------------------------------------------
 constexpr int64_t kMaxItems = int64_t(1) << 30;  // item indices stay in int32
@@ -1077,6 +1149,34 @@ cudaError_t copy_compact(void* compact, void* full, int64_t rows, int heads, int
   return cudaSuccess;
 }
 
+// The device address of [p, p + bytes) for a kernel on the current device:
+// page-locked host memory mapped into the device's address space (both ends
+// mapped, at device addresses `bytes - 1` apart), or — when `allow_device` —
+// device memory of the current device.  nullptr for anything else (pageable
+// host memory, another device's memory, an unknown pointer).
+void* mapped_range(const void* p, size_t bytes, bool allow_device) {
+  if (p == nullptr || bytes == 0) return nullptr;
+  int dev = 0;
+  cudaPointerAttributes first{}, last{};
+  const char* end = static_cast<const char*>(p) + (bytes - 1);
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaPointerGetAttributes(&first, p) != cudaSuccess ||
+      cudaPointerGetAttributes(&last, end) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  if (first.type == cudaMemoryTypeHost && last.type == cudaMemoryTypeHost) {
+    if (first.devicePointer == nullptr || last.devicePointer == nullptr) return nullptr;
+    const char* d0 = static_cast<const char*>(first.devicePointer);
+    const char* d1 = static_cast<const char*>(last.devicePointer);
+    if (size_t(d1 - d0) != bytes - 1) return nullptr;
+    return first.devicePointer;
+  }
+  if (allow_device && first.type == cudaMemoryTypeDevice && last.type == cudaMemoryTypeDevice &&
+      first.device == dev && last.device == dev)
+    return const_cast<void*>(p);
+  return nullptr;
+}
+
 }  // namespace
 
 extern "C" {
@@ -1094,6 +1194,8 @@ const char* welm_rope_status_string(int status) {
     case WELM_ROPE_ERR_CUDA: return "CUDA launch failed";
     case WELM_ROPE_ERR_TOO_MANY_TOKENS:
       return "n_tokens exceeds WELM_ROPE_STATIC_MAX_TOKENS (2048) of the static staging area; split the batch";
+    case WELM_ROPE_ERR_NOT_MAPPED:
+      return "a host buffer is not page-locked and mapped for the device (pin it, e.g. cudaHostAlloc or pin_memory)";
     default: return "unknown welm_rope status";
   }
 }
@@ -1343,6 +1445,45 @@ int welm_rope_ordinary_host_static(void* q, void* k, const int64_t* positions, c
     return WELM_ROPE_ERR_CUDA;
   }
   return WELM_ROPE_OK;
+}
+
+int welm_rope_ordinary_mapped(void* q, void* k, const int64_t* positions, const float* cos_sin_cache,
+                              int64_t n_tokens, int64_t q_token_stride, int64_t k_token_stride,
+                              int64_t max_position, int32_t* device_status, void* stream) {
+  if (n_tokens < 0 || max_position < 0 || n_tokens > kMaxItems / (kMappedPieces * kPieceThreads))
+    return WELM_ROPE_ERR_BAD_SIZE;
+  if (n_tokens == 0) return WELM_ROPE_OK;
+  if (!q || !k || !positions || !cos_sin_cache) return WELM_ROPE_ERR_NULL_POINTER;
+  if (n_tokens > 1 && (q_token_stride < kQHeads * kHeadDim || k_token_stride < kHeadDim))
+    return WELM_ROPE_ERR_BAD_STRIDE;
+  // 16-byte vectors everywhere: aligned bases and token strides of 8 elements
+  if (!aligned16(q) || !aligned16(k) || !aligned16(cos_sin_cache) ||
+      (n_tokens > 1 && (q_token_stride % 8 != 0 || k_token_stride % 8 != 0)))
+    return WELM_ROPE_ERR_BAD_STRIDE;
+  constexpr size_t kElem = sizeof(uint16_t);
+  const size_t q_bytes = (size_t(n_tokens - 1) * size_t(q_token_stride) + kQHeads * kHeadDim) * kElem;
+  const size_t k_bytes = (size_t(n_tokens - 1) * size_t(k_token_stride) + kHeadDim) * kElem;
+  void* dq = mapped_range(q, q_bytes, false);
+  void* dk = mapped_range(k, k_bytes, false);
+  void* dp = mapped_range(positions, size_t(n_tokens) * sizeof(int64_t), true);
+  if (dq == nullptr || dk == nullptr || dp == nullptr) return WELM_ROPE_ERR_NOT_MAPPED;
+
+  MappedArgs a{};
+  a.q = static_cast<uint16_t*>(dq);
+  a.k = static_cast<uint16_t*>(dk);
+  a.positions = static_cast<const int64_t*>(dp);
+  a.cache = cos_sin_cache;
+  a.q_stride = q_token_stride;
+  a.k_stride = k_token_stride;
+  a.max_position = max_position;
+  a.pieces = n_tokens * kMappedPieces;
+  a.threads = (a.pieces * kPieceThreads + 31) / 32 * 32;
+  a.status = device_status;
+  const int sms = current_sm_count();
+  const int64_t need = (a.threads + kMappedBlock - 1) / kMappedBlock;
+  const int64_t cap = sms > 0 ? int64_t(sms) * 32 : need;
+  return launch(rope_mapped_kernel, unsigned(need < cap ? need : cap), kMappedBlock, 0,
+                static_cast<cudaStream_t>(stream), a);
 }
 
 int welm_rope_count_tiles_host(const int64_t* seq_lens, int64_t batch_size,

@@ -3,18 +3,21 @@
 ``welmv4_inplace_rope_host(query, key, positions, cos_sin_cache)`` rotates
 host-resident Q ``[M, 6, 256]`` and K ``[M, 1, 256]`` (ordinary prefill /
 decode) in place with the B200 kernels.  Only the rotated lanes (192..255)
-cross PCIe — the op reads and writes nothing else — and the batch is split
-into chunks that flow through a three-stage pipeline on separate CUDA
-streams, so host->device copies, kernels and device->host copies of
-different chunks overlap (the two copy directions use different copy
-engines).  The call is stream-ordered like a device op: it starts after the
-work already queued on the current stream and the current stream waits for
-its last copy; the host tensors hold the result once the current stream is
-synchronised.  Host tensors should be pinned (``tensor.pin_memory()``) for
-the copies to be asynchronous.
+cross PCIe — the op reads and writes nothing else.  Two transports:
 
-The device staging buffers (three chunk slots) are allocated once per device
-and chunk size by this Python layer and reused; the C ABI underneath never
+* ``"mapped"`` (the default for pinned Q/K): one kernel
+  (``welm_rope_ordinary_mapped``) reads every 128-byte rope slice straight
+  from the pinned host tensors, rotates it and writes it back, so reads and
+  writes share the bus in both directions at once.  No staging, no copies.
+* ``"staged"`` (pageable Q/K, or on request): the batch is split into chunks
+  that flow through a three-stage pipeline on separate CUDA streams —
+  ``welm_rope_copy_rope_lanes`` in, the device kernel, copy back — with three
+  device staging slots allocated once per device and chunk size by this
+  Python layer.
+
+Either way the call is stream-ordered like a device op: it starts after the
+work already queued on the current stream, and the host tensors hold the
+result once the current stream is synchronised.  The C ABI underneath never
 allocates.
 """
 
@@ -110,18 +113,43 @@ def _check_host(t: torch.Tensor, name: str, dtype: torch.dtype, heads: Optional[
             raise ValueError(f"{name} must have contiguous heads and non-overlapping rows")
 
 
+def _mapped(query: torch.Tensor, key: torch.Tensor, positions: torch.Tensor, cos_sin_cache: torch.Tensor,
+            device: torch.device) -> None:
+    if positions.device.type == "cpu" and not (positions.is_pinned() and positions.is_contiguous()):
+        positions = positions.contiguous().to(device)  # the kernel reads pinned or device positions only
+    elif positions.device.type == "cuda":
+        positions = positions.contiguous()
+    stream = torch.cuda.current_stream(device)
+    with torch.cuda.device(device):
+        rc = _native.load().welm_rope_ordinary_mapped(
+            query.data_ptr(), key.data_ptr(), positions.data_ptr(), cos_sin_cache.data_ptr(),
+            int(positions.shape[0]), query.stride(0), key.stride(0), int(cos_sin_cache.shape[0]), None,
+            stream.cuda_stream)
+    _native.check("welm_rope_ordinary_mapped", rc)
+
+
+def _mappable(t: torch.Tensor) -> bool:
+    return (t.is_pinned() and t.data_ptr() % 16 == 0
+            and (t.shape[0] <= 1 or t.stride(0) % 8 == 0))
+
+
 def welmv4_inplace_rope_host(
     query: torch.Tensor,
     key: torch.Tensor,
     positions: torch.Tensor,
     cos_sin_cache: torch.Tensor,
     chunk_tokens: int = DEFAULT_CHUNK_TOKENS,
+    transport: str = "auto",
 ) -> None:
     """Ordinary prefill / decode RoPE on host-resident Q/K (see module doc).
 
     ``positions`` may be on the host or the device; ``cos_sin_cache`` lives on
-    the device that runs the op.
+    the device that runs the op.  ``transport`` is ``"auto"`` (mapped when Q
+    and K are pinned, 16-byte aligned with strides of 8 elements; staged
+    otherwise), ``"mapped"`` or ``"staged"``.
     """
+    if transport not in ("auto", "mapped", "staged"):
+        raise ValueError("transport must be 'auto', 'mapped' or 'staged'")
     if not isinstance(cos_sin_cache, torch.Tensor) or cos_sin_cache.device.type != "cuda":
         raise ValueError("cos_sin_cache must be a CUDA tensor (it selects the device)")
     _check_host(query, "query", torch.bfloat16, NUM_Q_HEADS)
@@ -132,7 +160,14 @@ def welmv4_inplace_rope_host(
     if query.shape[0] != n or key.shape[0] != n:
         raise ValueError("query, key and positions need the same row count")
     device = cos_sin_cache.device
-    key_ = (device.index if device.index is not None else torch.cuda.current_device(), int(chunk_tokens))
+    if device.index is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    if n == 0:
+        return
+    if transport == "mapped" or (transport == "auto" and _mappable(query) and _mappable(key)):
+        _mapped(query, key, positions, cos_sin_cache, device)
+        return
+    key_ = (device.index, int(chunk_tokens))
     with _lock:
         pipe = _pipelines.get(key_)
         if pipe is None:

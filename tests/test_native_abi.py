@@ -45,7 +45,7 @@ def test_every_declared_symbol_is_exported_and_bound():
 def test_abi_version_and_status_strings():
     lib = _native.load()
     assert lib.welm_rope_abi_version() >> 16 == 1
-    for code in range(7):
+    for code in range(9):
         assert _native.status_string(code)
     assert _native.status_string(99) == "unknown welm_rope status"
 
@@ -223,3 +223,32 @@ def test_kv_write_host_validation():
     assert f(css=100) == _native.ERR_BAD_STRIDE
     assert f(k=FAKE + 2) == _native.ERR_BAD_STRIDE  # 16-byte alignment required
     assert f(q=None, qo=None, k=None, v=None, p=None, c=None, li=None, sl=None, kc=None, vc=None, n=0) == _native.OK
+
+
+def test_mapped_entry_host_validation():
+    """Refusals happen on the host before any launch; FAKE pointers are never
+    reachable by a device, so even valid sizes end in ERR_NOT_MAPPED."""
+    lib = _native.load()
+    call = lib.welm_rope_ordinary_mapped
+    assert call(FAKE, FAKE, FAKE, FAKE, -1, 1536, 256, 16, None, None) == _native.ERR_BAD_SIZE
+    assert call(FAKE, FAKE, FAKE, FAKE, 4, 1536, 256, -1, None, None) == _native.ERR_BAD_SIZE
+    assert call(None, None, None, None, 0, 0, 0, 0, None, None) == _native.OK
+    assert call(None, FAKE, FAKE, FAKE, 4, 1536, 256, 16, None, None) == _native.ERR_NULL_POINTER
+    assert call(FAKE, FAKE, None, FAKE, 4, 1536, 256, 16, None, None) == _native.ERR_NULL_POINTER
+    assert call(FAKE, FAKE, FAKE, FAKE, 4, 1535, 256, 16, None, None) == _native.ERR_BAD_STRIDE
+    assert call(FAKE, FAKE, FAKE, FAKE, 4, 1540, 256, 16, None, None) == _native.ERR_BAD_STRIDE  # not 8-aligned
+    assert call(FAKE + 2, FAKE, FAKE, FAKE, 4, 1536, 256, 16, None, None) == _native.ERR_BAD_STRIDE
+    assert call(FAKE, FAKE, FAKE, FAKE + 4, 4, 1536, 256, 16, None, None) == _native.ERR_BAD_STRIDE
+    assert call(FAKE, FAKE, FAKE, FAKE, 4, 1536, 256, 16, None, None) == _native.ERR_NOT_MAPPED
+    assert "page-locked" in _native.status_string(_native.ERR_NOT_MAPPED)
+
+
+def test_host_entry_transport_argument():
+    import torch
+    from testfiles_b200 import host
+
+    q = torch.zeros((2, 6, 256), dtype=torch.bfloat16)
+    k = torch.zeros((2, 1, 256), dtype=torch.bfloat16)
+    pos = torch.zeros(2, dtype=torch.int64)
+    with pytest.raises(ValueError, match="transport"):
+        host.welmv4_inplace_rope_host(q, k, pos, torch.zeros((8, 64)), transport="zero-copy")
