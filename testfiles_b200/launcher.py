@@ -1,7 +1,8 @@
 """Launch / time any catalogue case of the in-place RoPE (profiling launcher).
 
     python -m testfiles_b200.launcher --cases b_mirror_segmented_n16384_bs128_uneven --iters 20
-    python -m testfiles_b200.launcher --cases baseline --time --json gpurun_out/times.jsonl
+    python -m testfiles_b200.launcher --cases baseline --time --json times.jsonl
+    python -m testfiles_b200.launcher --cases b_prefill_m16384 --host mapped
 
 ``--iters N`` launches the op N times eagerly on one buffer set with a fixed
 kernel name per path (``rope_ordinary_kernel`` / ``rope_mirror_kernel``), for
@@ -16,7 +17,14 @@ record states), CUDA events on the launching stream, median of 5 trials.
 Each record is one JSON line whose fields follow the reference's CSV record
 (bench_welmv4_inplace_rope_npu.py:1143-1162,1529-1540): ``record_type``,
 case fields, then µs per launch, tokens/s, GB/s of algorithmic bytes and the
-fraction of the HBM peak.
+fraction of the HBM peak.  ``--copy-ceiling`` adds the time of a plain device
+copy moving the same bytes (half read, half written), replayed and rotated
+exactly like the op: the practical ceiling at that size, where launch and
+pipeline-fill costs weigh as much as bandwidth.
+
+``--host mapped|staged`` times the host-memory entry instead (ordinary
+cases): Q, K and positions in pinned host memory, every PCIe transfer inside
+the timed region, µs per call and GB/s each way over the bus.
 """
 
 from __future__ import annotations
@@ -98,8 +106,43 @@ def _with_lens(case: workloads.Case, inp: workloads.Inputs, device: torch.device
     return inp
 
 
+def _replay_us(graph: "torch.cuda.CUDAGraph", device: torch.device, trials: int, replays: int,
+               graph_launches: int) -> float:
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize(device)
+    stream = torch.cuda.current_stream(device)
+    samples = []
+    for _ in range(trials):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(replays):
+            graph.replay()
+        end.record(stream)
+        end.synchronize()
+        samples.append(start.elapsed_time(end) * 1e3 / (replays * graph_launches))
+    return statistics.median(samples)
+
+
+def same_size_copy_us(nbytes: int, sets: int, device: torch.device, trials: int = 5, graph_launches: int = 64,
+                      replays: int = 20) -> float:
+    """µs per device copy of ``nbytes // 2`` bytes (``nbytes`` of traffic),
+    graph-replayed over ``sets`` rotating source/destination pairs."""
+    half = max(16, nbytes // 2 // 16 * 16)
+    pairs = [(torch.ones(half, dtype=torch.uint8, device=device), torch.empty(half, dtype=torch.uint8, device=device))
+             for _ in range(sets)]
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(graph_launches):
+            src, dst = pairs[i % sets]
+            dst.copy_(src)
+    us = _replay_us(graph, device, trials, replays, graph_launches)
+    del graph, pairs
+    return us
+
+
 def time_case(case: workloads.Case, device: torch.device, trials: int = 5, graph_launches: int = 64,
-              replays: Optional[int] = None, from_lens: bool = False) -> dict:
+              replays: Optional[int] = None, from_lens: bool = False, copy_ceiling: bool = False) -> dict:
     """µs per launch of ``case`` (graph-replayed over rotating buffer sets);
     ``from_lens`` runs segmented mirror cases through rope_mirror_from_lens."""
     host = workloads.make_inputs(case, "cpu")
@@ -122,26 +165,17 @@ def time_case(case: workloads.Case, device: torch.device, trials: int = 5, graph
     with torch.cuda.graph(graph):
         for i in range(graph_launches):
             _launch(buffers[i % sets])
-    for _ in range(3):
-        graph.replay()
-    torch.cuda.synchronize(device)
     if replays is None:  # about 5 ms of launches per trial
         est_us = 1.5 + nbytes / 5e6
         replays = max(5, min(200, int(5e3 / (est_us * graph_launches))))
-    stream = torch.cuda.current_stream(device)
-    samples = []
-    for _ in range(trials):
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record(stream)
-        for _ in range(replays):
-            graph.replay()
-        end.record(stream)
-        end.synchronize()
-        samples.append(start.elapsed_time(end) * 1e3 / (replays * graph_launches))
-    del graph
-    us = statistics.median(samples)
+    us = _replay_us(graph, device, trials, replays, graph_launches)
+    del graph, buffers
     peak, kind = measured_hbm_peak()
     gbs = nbytes / (us * 1e3)
+    ceiling = {}
+    if copy_ceiling:
+        copy_us = same_size_copy_us(nbytes, sets, device, trials, graph_launches, replays)
+        ceiling = {"same_size_copy_us": round(copy_us, 3), "frac_of_same_size_copy": round(copy_us / us, 4)}
     return {
         "record_type": "timing",
         **case_fields(case),
@@ -153,6 +187,7 @@ def time_case(case: workloads.Case, device: torch.device, trials: int = 5, graph
         "hbm_peak_gbs": peak,
         "hbm_peak_source": kind,
         "hbm_frac_of_8tbs_spec": round(gbs / SPEC_HBM_GBS, 4),
+        **ceiling,
         "buffer_sets": sets,
         "l2_cold": bool(sets * nbytes > 2 * L2_BYTES),
         "pdl": os.environ.get("WELM_ROPE_PDL", "1") != "0",
@@ -161,6 +196,47 @@ def time_case(case: workloads.Case, device: torch.device, trials: int = 5, graph
         "device_name": torch.cuda.get_device_name(device),
         "torch_version": torch.__version__,
         "python_version": platform.python_version(),
+    }
+
+
+def time_host_case(case: workloads.Case, device: torch.device, transport: str, trials: int = 5,
+                   calls: int = 20) -> dict:
+    """µs per call of the host-memory entry (``welmv4_inplace_rope_host``)
+    on pinned host Q/K/positions for an ordinary case, every transfer
+    inside the timed region (CUDA events on the current stream)."""
+    from . import host as welm_host
+
+    if case.is_mirror:
+        raise ValueError("the host-memory entry serves ordinary prefill / decode cases")
+    inp = workloads.make_inputs(case, "cpu")
+    q, k, pos = inp.query.pin_memory(), inp.key.pin_memory(), inp.positions.pin_memory()
+    cache = inp.cache.to(device)
+    for _ in range(3):
+        welm_host.welmv4_inplace_rope_host(q, k, pos, cache, transport=transport)
+    torch.cuda.synchronize(device)
+    stream = torch.cuda.current_stream(device)
+    samples = []
+    for _ in range(trials):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(calls):
+            welm_host.welmv4_inplace_rope_host(q, k, pos, cache, transport=transport)
+        end.record(stream)
+        end.synchronize()
+        samples.append(start.elapsed_time(end) * 1e3 / calls)
+    us = statistics.median(samples)
+    h2d, d2h = welm_host.lane_bytes(case.n_tokens)
+    return {
+        "record_type": "host_timing",
+        **case_fields(case),
+        "transport": transport,
+        "us_per_call": round(us, 2),
+        "tokens_per_s": round(case.n_tokens / (us * 1e-6), 1),
+        "h2d_bytes_per_call": h2d,
+        "d2h_bytes_per_call": d2h,
+        "pcie_gb_s_each_way": round(d2h / (us * 1e3), 2),
+        "gb_s_algorithmic": round(workloads.min_bytes(case) / (us * 1e3), 2),
+        "device_name": torch.cuda.get_device_name(device),
     }
 
 
@@ -176,13 +252,18 @@ def launch_case(case: workloads.Case, device: torch.device, iters: int, from_len
 
 
 def run(cases: Iterable[workloads.Case], device: torch.device, time_it: bool, iters: int,
-        out: Optional[str], from_lens: bool = False) -> list[dict]:
+        out: Optional[str], from_lens: bool = False, copy_ceiling: bool = False,
+        host_transport: Optional[str] = None) -> list[dict]:
     records = []
     sink = open(out, "a") if out else None
     try:
         for case in cases:
-            rec = (time_case(case, device, from_lens=from_lens) if time_it
-                   else launch_case(case, device, iters, from_lens))
+            if host_transport is not None:
+                rec = time_host_case(case, device, host_transport)
+            elif time_it:
+                rec = time_case(case, device, from_lens=from_lens, copy_ceiling=copy_ceiling)
+            else:
+                rec = launch_case(case, device, iters, from_lens)
             records.append(rec)
             line = json.dumps(rec)
             print(line, flush=True)
@@ -205,13 +286,18 @@ def main(argv: Optional[list[str]] = None) -> int:
     parser.add_argument("--json", default=None, help="append JSON lines here")
     parser.add_argument("--mirror-from-lens", action="store_true",
                         help="run segmented KV-mirror cases through rope_mirror_from_lens")
+    parser.add_argument("--copy-ceiling", action="store_true",
+                        help="with --time: also time a same-size device copy (the practical ceiling)")
+    parser.add_argument("--host", choices=("mapped", "staged"), default=None,
+                        help="time the host-memory entry on pinned Q/K with this transport (ordinary cases)")
     args = parser.parse_args(argv)
     if not torch.cuda.is_available():
         print("the launcher needs a CUDA device", file=sys.stderr)
         return 2
     device = torch.device(args.device)
     torch.cuda.set_device(device)
-    run(select_cases(args.cases), device, args.time, args.iters, args.json, args.mirror_from_lens)
+    run(select_cases(args.cases), device, args.time, args.iters, args.json, args.mirror_from_lens,
+        args.copy_ceiling, args.host)
     return 0
 
 

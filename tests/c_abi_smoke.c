@@ -6,8 +6,10 @@
  *
  * Covers: welm_rope_ordinary (dense and segmented), welm_rope_mirror
  * (segmented), welm_rope_build_tiles (device) against welm_rope_build_tiles_host
- * and the oracle builder, host-side validation (a NULL pointer is refused with
- * its status string) and the device status word staying zero.
+ * and the oracle builder, welm_rope_ordinary_mapped on page-locked host
+ * buffers (and its refusal of pageable ones), host-side validation (a NULL
+ * pointer is refused with its status string) and the device status word
+ * staying zero.
  *
  * Exit status 0 = every check passed.  Built and run by tests/test_c_abi.py.
  */
@@ -215,6 +217,47 @@ static void check_mirror(const float* cache, const float* d_cache) {
   free(q); free(k); free(q_want); free(k_want); free(q_got); free(k_got); free(pos);
 }
 
+/* Q/K stay in page-locked host memory; the kernel reads and writes them over
+ * the bus.  Positions are host memory too. */
+static void check_mapped(const float* cache, const float* d_cache, int64_t n) {
+  const size_t qn = (size_t)n * NQ * HD, kn = (size_t)n * HD;
+  uint16_t *q = NULL, *k = NULL;
+  int64_t* pos = NULL;
+  CHECK_CUDA(cudaMallocHost((void**)&q, qn * 2));
+  CHECK_CUDA(cudaMallocHost((void**)&k, kn * 2));
+  CHECK_CUDA(cudaMallocHost((void**)&pos, (size_t)n * 8));
+  uint16_t* q_want = malloc(qn * 2);
+  uint16_t* k_want = malloc(kn * 2);
+  for (size_t i = 0; i < qn; ++i) q[i] = random_bf16();
+  for (size_t i = 0; i < kn; ++i) k[i] = random_bf16();
+  for (int64_t i = 0; i < n; ++i) pos[i] = (int64_t)(next_u32() % MAX_POS);
+  EXPECT(welm_oracle_apply(q, q_want, n, NQ, NQ * HD, pos, cache, MAX_POS) == 0, "oracle positions in range");
+  EXPECT(welm_oracle_apply(k, k_want, n, 1, HD, pos, cache, MAX_POS) == 0, "oracle positions in range");
+
+  /* pageable memory is refused before anything is launched */
+  uint16_t* pageable = malloc(qn * 2);
+  memcpy(pageable, q, qn * 2);
+  int rc = welm_rope_ordinary_mapped(pageable, k, pos, d_cache, n, NQ * HD, HD, MAX_POS, NULL, NULL);
+  EXPECT(rc == WELM_ROPE_ERR_NOT_MAPPED, "pageable Q is refused");
+  EXPECT(memcmp(pageable, q, qn * 2) == 0, "refused call wrote nothing");
+
+  int32_t zero = 0, status = -1;
+  int32_t* dstatus = device_copy(&zero, 4);
+  rc = welm_rope_ordinary_mapped(q, k, pos, d_cache, n, NQ * HD, HD, MAX_POS, dstatus, NULL);
+  EXPECT(rc == WELM_ROPE_OK, welm_rope_status_string(rc));
+  CHECK_CUDA(cudaDeviceSynchronize());
+  CHECK_CUDA(cudaMemcpy(&status, dstatus, 4, cudaMemcpyDeviceToHost));
+  EXPECT(same_bits(q, q_want, qn, "mapped Q"), "mapped Q");
+  EXPECT(same_bits(k, k_want, kn, "mapped K"), "mapped K");
+  EXPECT(status == 0, "device status stays zero");
+
+  CHECK_CUDA(cudaFree(dstatus));
+  CHECK_CUDA(cudaFreeHost(q));
+  CHECK_CUDA(cudaFreeHost(k));
+  CHECK_CUDA(cudaFreeHost(pos));
+  free(pageable); free(q_want); free(k_want);
+}
+
 int main(void) {
   EXPECT(welm_rope_abi_version() >> 16 == 1, "ABI major version 1");
   /* host validation happens before any CUDA call and names the problem */
@@ -233,6 +276,7 @@ int main(void) {
   check_ordinary(cache, d_cache, 1000, 0);
   check_ordinary(cache, d_cache, 777, 1);
   check_mirror(cache, d_cache);
+  check_mapped(cache, d_cache, 1234);
 
   CHECK_CUDA(cudaFree(d_cache));
   free(cache);

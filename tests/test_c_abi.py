@@ -1,9 +1,9 @@
 """A plain C program as the caller of the C ABI.
 
 tests/c_abi_smoke.c binds include/welm_rope.h the way a C or cgo host would
-(no torch; the CUDA runtime only for device memory) and checks the ordinary,
-segmented and KV-mirror entries and both tile builders bit for bit against
-the C oracle (oracle/rope_oracle.c).  On CPU the program must compile as C99
+(no torch; the CUDA runtime only for device and page-locked host memory) and
+checks the ordinary, segmented, KV-mirror and mapped-host entries and both
+tile builders bit for bit against the C oracle (oracle/rope_oracle.c).  On CPU the program must compile as C99
 and link against every symbol it uses; on a B200 it must run and pass.
 """
 
