@@ -63,15 +63,19 @@ def _reported_failure(rank: int, world: int, port: int, queue) -> None:
 def _dead_rank(rank: int, world: int, port: int, queue) -> None:
     from testfiles_b200 import sharding
 
-    _init(rank, world, port)
-    if rank == 1:
-        os._exit(7)  # dies between steps: nothing of it is in flight
-    t0 = time.monotonic()
+    phase, t0 = "init", time.monotonic()
     try:
+        _init(rank, world, port)
+        phase = "first step"
+        dist.barrier()  # both ranks are fully connected and one step is done
+        if rank == 1:
+            time.sleep(0.5)  # let the survivor enter its next collective
+            os._exit(7)  # dies between steps: nothing of it is in flight
+        phase, t0 = "status step", time.monotonic()
         sharding.check_all_ranks(0)
-        queue.put((rank, "no error", time.monotonic() - t0))
+        queue.put((rank, phase, "no error", time.monotonic() - t0))
     except Exception as err:  # gloo reports a closed peer or a timeout
-        queue.put((rank, type(err).__name__, time.monotonic() - t0))
+        queue.put((rank, phase, type(err).__name__, time.monotonic() - t0))
     os._exit(0)  # the group cannot be torn down cleanly with a peer gone
 
 
@@ -115,8 +119,8 @@ def test_reported_failure_reaches_every_rank_and_skips_the_gather():
 
 def test_dead_rank_ends_the_survivors_collective_with_an_error():
     results, codes = _run(_dead_rank)
-    (rank, outcome, elapsed), = results
-    assert rank == 0 and outcome != "no error"
+    (rank, phase, outcome, elapsed), = results
+    assert (rank, phase) == (0, "status step") and outcome != "no error"
     assert elapsed < 60, f"the survivor waited {elapsed:.0f} s"
     assert codes == [0, 7]
 
