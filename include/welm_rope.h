@@ -284,7 +284,10 @@ int welm_rope_ordinary_mapped(void* q, void* k, const int64_t* positions,
 /* Human-readable name of a welm_rope_status code (static storage). */
 const char* welm_rope_status_string(int status);
 
-/* ABI version of this header: (major << 16) | minor. */
+/* ABI version of this header: (major << 16) | minor.  A minor bump only adds
+ * entry points or status codes; a major bump changes an existing signature.
+ * 1.1 added welm_rope_ordinary_mapped and WELM_ROPE_ERR_NOT_MAPPED. */
+#define WELM_ROPE_ABI_VERSION ((1 << 16) | 1)
 int welm_rope_abi_version(void);
 
 #ifdef __cplusplus

@@ -1181,7 +1181,7 @@ void* mapped_range(const void* p, size_t bytes, bool allow_device) {
 
 extern "C" {
 
-int welm_rope_abi_version(void) { return (1 << 16) | 0; }
+int welm_rope_abi_version(void) { return WELM_ROPE_ABI_VERSION; }
 
 const char* welm_rope_status_string(int status) {
   switch (status) {

@@ -259,7 +259,7 @@ static void check_mapped(const float* cache, const float* d_cache, int64_t n) {
 }
 
 int main(void) {
-  EXPECT(welm_rope_abi_version() >> 16 == 1, "ABI major version 1");
+  EXPECT(welm_rope_abi_version() == WELM_ROPE_ABI_VERSION, "library and header ABI versions agree");
   /* host validation happens before any CUDA call and names the problem */
   const int bad = welm_rope_ordinary(NULL, NULL, NULL, NULL, NULL, 1, 4, NQ * HD, HD, 0, MAX_POS, NULL, NULL);
   EXPECT(bad == WELM_ROPE_ERR_NULL_POINTER, "NULL q is refused");

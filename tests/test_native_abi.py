@@ -45,6 +45,9 @@ def test_every_declared_symbol_is_exported_and_bound():
 def test_abi_version_and_status_strings():
     lib = _native.load()
     assert lib.welm_rope_abi_version() >> 16 == 1
+    header = (REPO / "include" / "welm_rope.h").read_text()
+    major, minor = map(int, re.search(r"#define WELM_ROPE_ABI_VERSION \(\((\d+) << 16\) \| (\d+)\)", header).groups())
+    assert lib.welm_rope_abi_version() == (major << 16) | minor
     for code in range(9):
         assert _native.status_string(code)
     assert _native.status_string(99) == "unknown welm_rope status"

@@ -76,6 +76,8 @@ def _dead_rank(rank: int, world: int, port: int, queue) -> None:
         queue.put((rank, phase, "no error", time.monotonic() - t0))
     except Exception as err:  # gloo reports a closed peer or a timeout
         queue.put((rank, phase, type(err).__name__, time.monotonic() - t0))
+    queue.close()
+    queue.join_thread()  # the report must reach the pipe before the hard exit below
     os._exit(0)  # the group cannot be torn down cleanly with a peer gone
 
 
