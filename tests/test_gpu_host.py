@@ -30,7 +30,7 @@ def host_inputs(m: int, seed: int, pin: bool = True):
 
 @pytest.mark.parametrize("transport", ["mapped", "staged"])
 @pytest.mark.parametrize("m,chunk", [(1, 2048), (100, 2048), (2048, 2048), (5000, 2048), (777, 64), (9000, 1000),
-                                     (16384, 2048)])
+                                     (16384, 2048), (40000, 4096)])  # 40000: the mapped grid strides twice
 def test_host_entry_matches_oracle(m, chunk, transport):
     q, k, pos, cache = host_inputs(m, m)
     q0, k0 = q.clone(), k.clone()
