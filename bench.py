@@ -392,7 +392,7 @@ def run_b200_arm(args) -> int:
         # Same-size copy ceiling: a plain device copy moving the same number of
         # bytes per step (half read, half written), replayed and timed exactly
         # like the op, over rotating buffers larger than L2.
-        half = algorithmic_bytes(TOKENS) // 2 // 16 * 16
+        half = algorithmic_bytes(TOKENS) // 2 // 4096 * 4096  # 4 KiB multiple: the copy's fast path
         pairs = [(torch.empty(half, dtype=torch.uint8, device=device).fill_(1),
                   torch.empty(half, dtype=torch.uint8, device=device)) for _ in range(BUFFER_SETS)]
         copy_graph = torch.cuda.CUDAGraph()
