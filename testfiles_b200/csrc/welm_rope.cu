@@ -294,17 +294,21 @@ struct RowGather {
 // (bench_welmv4_inplace_rope_npu.py:700-718, 856-867): tile i covers
 // [starts[i], starts[i] + min(64, starts[i+1] - starts[i])).
 //   kDense:     has_segments = 0; token = slot, slots = min(N, 64 * tiles).
-//   kTileTable: has_segments = 1 with a table that fits in shared memory;
+//   kTileTable: has_segments = 1 with at most kTableCap table entries;
 //               items are tokens 0..N-1 in order, so every load is issued at
-//               once, and a token is rotated iff a tile covers it (binary
-//               search of the staged table, done while the loads fly).
-//               Exact for any non-decreasing table; other tables are flagged.
+//               once, and a token is rotated iff a tile covers it (ordinary:
+//               binary search of the table staged in shared memory; mirror:
+//               a warp-cooperative search of the global table while the
+//               loads fly).  Exact for any non-decreasing table; other tables
+//               are flagged.
 //   kTileSlots: has_segments = 1 with a large table; 64 slots per tile,
 //               token = starts[tile] + slot (one extra dependent load).
 // ---------------------------------------------------------------------------
 enum class Source { kDense, kTileTable, kTileSlots };
 
 constexpr int kTableCap = 2048;  // staged table entries (8 KB of shared memory)
+// warp_table_covers searches two levels of at most 32 x 64 entries
+static_assert(kTableCap <= 32 * 64, "the warp search covers at most 2048 table entries");
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -335,6 +339,33 @@ __device__ __forceinline__ bool table_covers(const int32_t* s_tab, int num_tiles
   }
   const int i = lo - 1;
   return i >= 0 && i < num_tiles && t - s_tab[i] < kTile;
+}
+
+// Warp-cooperative coverage test on the global tile table (read-only path;
+// its lines were prefetched into L2 in the PDL window and are read only after
+// the wait): a 32-way ballot search finds the last entry at or before the
+// warp's first token t_ref in two rounds of parallel loads (instead of
+// log2(T) dependent ones), then each lane steps forward to its own token
+// t >= t_ref.  Same answer as table_covers for every non-decreasing table;
+// for other tables (flagged by the check items) the answer is arbitrary, but
+// every index read stays in [0, num_tiles].  All 32 lanes must call it.
+__device__ __forceinline__ bool warp_table_covers(const int32_t* g_tab, int num_tiles, int64_t t_ref, int64_t t) {
+  constexpr unsigned kAll = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
+  const int entries = num_tiles + 1;
+  const int stride = (entries + 31) >> 5;
+  const int e0 = lane * stride;
+  const int blocks = __popc(__ballot_sync(kAll, e0 < entries && __ldg(g_tab + e0) <= t_ref));
+  int i = -1;
+  if (blocks > 0) {  // warp-uniform
+    const int base = (blocks - 1) * stride;
+    const int e1 = base + lane, e2 = base + 32 + lane;
+    const bool le1 = lane < stride && e1 < entries && __ldg(g_tab + e1) <= t_ref;
+    const bool le2 = 32 + lane < stride && e2 < entries && __ldg(g_tab + e2) <= t_ref;
+    i = base + __popc(__ballot_sync(kAll, le1)) + __popc(__ballot_sync(kAll, le2)) - 1;
+  }
+  while (i < num_tiles && __ldg(g_tab + i + 1) <= t) ++i;
+  return i >= 0 && i < num_tiles && t - __ldg(g_tab + i) < kTile;
 }
 
 // Tile validation item: flags a tile that starts below 0, ends past N, runs
@@ -489,7 +520,6 @@ __device__ __forceinline__ void mirror_k_token(const RopeArgs& a, int64_t tok, i
 // At most 128 registers: 4 CTAs per SM keep a 16384-token launch in one wave.
 template <bool kVec, Source kSrc>
 __global__ void __launch_bounds__(kBlock, 4) rope_mirror_kernel(const RopeArgs a) {
-  extern __shared__ int32_t s_tab[];
   // warm the first item's cos/sin row (Q rows: through a last_index hint)
   const int item0 = blockIdx.x * blockDim.x + threadIdx.x;
   int64_t src_hint = -1, pos_hint = -1;
@@ -504,10 +534,9 @@ __global__ void __launch_bounds__(kBlock, 4) rope_mirror_kernel(const RopeArgs a
   pdl_enter();
   if constexpr (kSrc == Source::kTileTable) {
     // One item per thread: Q rows, then tokens [0, k_items / 4), then one
-    // check per tile.  Every thread reaches the single barrier below in
-    // uniform control flow: phase 1 issues the loads of whatever item the
-    // thread owns, phase 2 finishes it.
-    stage_table_async(s_tab, a.tile_starts, a.num_tiles + 1);
+    // check per tile.  Phase 1 issues the loads of whatever item the thread
+    // owns; the coverage search (warp-uniform, no barrier) runs while they
+    // fly; phase 2 finishes the item.
     const int item = blockIdx.x * blockDim.x + threadIdx.x;
     const int part = item & (kParts - 1);
     const bool is_q = item < a.q_items;
@@ -517,25 +546,26 @@ __global__ void __launch_bounds__(kBlock, 4) rope_mirror_kernel(const RopeArgs a
     Slices<kVec, kQHeads> qx;
     Slices<kVec, 1> kx;
     RowGather<kVec> g;
-    bool pos_ok = false;
-    int64_t src = 0;
+    int64_t src = 0, pos = 0;
     if (is_q) {
       qx.load(a.q + int64_t(item >> kPartShift) * a.q_stride, part);
       src = __ldg(a.last_index + (item >> kPartShift));
       g.issue(a, src_hint, pos_hint, part);
     } else if (is_token) {
-      const int64_t pos = __ldg(a.positions + tok);
+      pos = __ldg(a.positions + tok);
       kx.load(a.k + tok * a.k_stride, part);
       g.issue(a, -1, pos_hint, part);
-      pos_ok = g.finish(a, pos, part);
     } else if (k_item - a.k_items < a.num_tiles) {
       check_tile(a, k_item - a.k_items);
     }
-    stage_table_wait();
+    // the coverage search runs while the loads above are in flight
+    const int first_k = max(item & ~31, a.q_items) - a.q_items;  // the warp's first K item
+    const int64_t t_ref = first_k < a.k_items ? int64_t(first_k >> kPartShift) : 0;
+    const bool covered = warp_table_covers(a.tile_starts, a.num_tiles, t_ref, is_token ? tok : t_ref);
     if (is_q) {
       finish_q_row<kVec>(a, qx, src, g, part);
-    } else if (is_token && table_covers(s_tab, a.num_tiles, tok)) {
-      if (pos_ok) {
+    } else if (is_token && covered) {
+      if (g.finish(a, pos, part)) {
         kx.rotate_store(g.cs);
       } else if (part == 0) {
         raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
@@ -1076,10 +1106,10 @@ Plan plan_tokens(int64_t has_segments, int64_t num_work_tiles, int64_t n_tokens)
 }
 
 template <typename Kernel>
-int launch_plan(Kernel kernel, const Plan& plan, const RopeArgs& a, cudaStream_t stream) {
+int launch_plan(Kernel kernel, const Plan& plan, const RopeArgs& a, cudaStream_t stream, bool staged_table = true) {
   const int64_t total = int64_t(a.q_items) + plan.token_items + plan.check_items;
   if (plan.src == Source::kTileTable) {
-    const size_t smem = (size_t(a.num_tiles + 1) * sizeof(int32_t) + 15) & ~size_t(15);
+    const size_t smem = staged_table ? (size_t(a.num_tiles + 1) * sizeof(int32_t) + 15) & ~size_t(15) : 0;
     return launch(kernel, unsigned((total + kBlock - 1) / kBlock), kBlock, smem, stream, a);
   }
   return launch(kernel, grid_for(total), kBlock, 0, stream, a);
@@ -1098,7 +1128,7 @@ template <bool kVec>
 int launch_mirror(const Plan& plan, const RopeArgs& a, cudaStream_t s) {
   switch (plan.src) {
     case Source::kDense: return launch_plan(rope_mirror_kernel<kVec, Source::kDense>, plan, a, s);
-    case Source::kTileTable: return launch_plan(rope_mirror_kernel<kVec, Source::kTileTable>, plan, a, s);
+    case Source::kTileTable: return launch_plan(rope_mirror_kernel<kVec, Source::kTileTable>, plan, a, s, false);
     default: return launch_plan(rope_mirror_kernel<kVec, Source::kTileSlots>, plan, a, s);
   }
 }
