@@ -25,6 +25,10 @@ cos/sin cache [16384, 64] (rotary base 1e4), seeded N(0,1) synthetic data.
   measured HBM copy peak.
 * ``cpu_baseline`` (rank 0, N=1 only): the reference's CPU algorithm (the
   oracle port of its torch path) on this host's cores, same workload.
+* ``other_configs`` (rank 0, N=1 only): one configuration of each other
+  judged family (prefill M=8192, decode M=1 and M=128, contiguous and
+  segmented KV mirror at N=16384) timed after the headline, with a same-size
+  device copy beside each (``--no-config-sweep`` skips it).
 
 ``--impl reference`` times the reference's CPU implementation alone (rank 0;
 other ranks exit 0).  Multi-GPU runs (torchrun) shard requests: each rank
@@ -284,6 +288,26 @@ def timed_steps(step, count: int, dist, device, stream) -> float:
     return max_over_ranks(dist, start.elapsed_time(end), device)
 
 
+# One configuration of each other judged family, timed after the headline
+# (rank 0, N=1) with the launcher's method: graph replay over L2-cold buffer
+# sets, plus a same-size device copy as the practical ceiling.
+OTHER_CONFIGS = ("b_prefill_m8192", "b_decode_m1", "b_decode_m128", "b_mirror_contiguous_n16384",
+                 "b_mirror_segmented_n16384_bs128_uneven")
+
+
+def other_config_records(device) -> list[dict]:
+    from testfiles_b200 import launcher, workloads
+
+    keep = ("case", "phase", "n_tokens", "batch_size", "us_per_launch", "gb_s", "hbm_frac", "same_size_copy_us",
+            "frac_of_same_size_copy", "l2_cold")
+    launcher.time_case(workloads.find_case(OTHER_CONFIGS[0]), device, trials=1)  # warm-up, discarded
+    out = []
+    for name in OTHER_CONFIGS:
+        rec = launcher.time_case(workloads.find_case(name), device, copy_ceiling=True)
+        out.append({k: rec[k] for k in keep})
+    return out
+
+
 def run_b200_arm(args) -> int:
     import testfiles_b200 as welm
     from testfiles_b200 import host as welm_host
@@ -418,6 +442,7 @@ def run_b200_arm(args) -> int:
     line = None
     if rank == 0:
         cpu = None
+        others = other_config_records(device) if world == 1 and not args.no_config_sweep else None
         if world == 1:
             times, threads = cpu_reference_time(host, runs=5)
             cpu_t = statistics.median(times)
@@ -493,6 +518,7 @@ def run_b200_arm(args) -> int:
             },
             "clocks": sampler.summary(),
             "gpu_launches": launches,
+            "other_configs": others,
             "gpu_launches_e2e": launches_e2e,
         }
     if dist is not None:
@@ -509,6 +535,8 @@ def main() -> int:
     parser.add_argument("--steps", type=int, default=20000)
     parser.add_argument("--warmup", type=int, default=50)
     parser.add_argument("--e2e-steps", type=int, default=100)
+    parser.add_argument("--no-config-sweep", action="store_true",
+                        help="skip the one-per-family timing of the other judged configurations")
     parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
     args = parser.parse_args()
     if args.steps <= 0:
