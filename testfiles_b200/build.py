@@ -1,7 +1,7 @@
 """Build recipe for the in-tree sm_100a shared library.
 
-``python -m testfiles_b200.build`` (or ``build_native()``) compiles
-``csrc/welm_rope.cu`` with nvcc for ``sm_100a`` only into
+``python -m testfiles_b200.build`` (or ``build_native()``) compiles the
+``csrc/*.cu`` translation units with nvcc for ``sm_100a`` only into
 ``testfiles_b200/libwelm_rope_b200.so``.  The CUDA runtime is linked
 statically, so the library loads on a machine without a GPU (the host-only
 entry points then work; the device ones report a CUDA error).
@@ -17,8 +17,12 @@ from pathlib import Path
 
 PACKAGE_DIR = Path(__file__).resolve().parent
 REPO_ROOT = PACKAGE_DIR.parent
-SOURCES = (PACKAGE_DIR / "csrc" / "welm_rope.cu",)
-HEADERS = (REPO_ROOT / "include" / "welm_rope.h",)
+CSRC = PACKAGE_DIR / "csrc"
+# one translation unit per kernel family; the .cuh headers hold what they share
+SOURCES = tuple(CSRC / name for name in (
+    "rope_ordinary.cu", "rope_mirror.cu", "rope_kv_write.cu", "rope_tiles.cu", "rope_host_memory.cu",
+    "rope_abi.cu"))
+HEADERS = (REPO_ROOT / "include" / "welm_rope.h", CSRC / "rope_device.cuh", CSRC / "rope_host.cuh")
 LIBRARY = PACKAGE_DIR / "libwelm_rope_b200.so"
 
 NVCC_FLAGS = (

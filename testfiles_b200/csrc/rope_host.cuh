@@ -1,0 +1,107 @@
+// rope_host.cuh — host-side launch plumbing shared by the C entry points:
+// SM count, grid sizing, the PDL launch wrapper and the token-source plan.
+
+#ifndef WELM_ROPE_HOST_CUH_
+#define WELM_ROPE_HOST_CUH_
+
+#include <atomic>
+#include <cstdlib>
+#include <utility>
+
+#include "rope_device.cuh"
+
+namespace {
+// ---------------------------------------------------------------------------
+// Host side.
+// ---------------------------------------------------------------------------
+constexpr int64_t kMaxItems = int64_t(1) << 30;  // item indices stay in int32
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int current_sm_count() {
+  static std::atomic<int> cache[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return 0;
+  if (dev < kMaxDevices) {
+    const int v = cache[dev].load(std::memory_order_relaxed);
+    if (v > 0) return v;
+  }
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  if (dev < kMaxDevices) cache[dev].store(sms, std::memory_order_relaxed);
+  return sms;
+}
+
+// Grid for `items` work items of a grid-stride kernel: enough CTAs for one
+// item per thread, capped at 16 CTAs of 128 threads per SM (more than these
+// kernels keep resident) so larger inputs loop.
+unsigned grid_for(int64_t items) {
+  const int sms = current_sm_count();
+  const int64_t need = (items + kBlock - 1) / kBlock;
+  const int64_t cap = sms > 0 ? int64_t(sms) * 16 : need;
+  return unsigned(need < cap ? need : cap);
+}
+
+// Launches carry the programmatic-stream-serialization attribute (PDL) unless
+// the environment sets WELM_ROPE_PDL=0: the grid may be scheduled while the
+// previous kernel in the stream drains, and waits in pdl_enter() before it
+// touches memory.
+bool pdl_enabled() {
+  static const bool enabled = [] {
+    const char* v = std::getenv("WELM_ROPE_PDL");
+    return !(v != nullptr && v[0] == '0');
+  }();
+  return enabled;
+}
+
+template <typename... Params, typename... Args>
+int launch(void (*kernel)(Params...), unsigned grid, unsigned block, size_t smem, cudaStream_t stream,
+           Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (err != cudaSuccess) {
+    cudaGetLastError();  // clear the launch error so later calls start clean
+    return WELM_ROPE_ERR_CUDA;
+  }
+  return WELM_ROPE_OK;
+}
+
+// How the token phase is laid out for one call (see Source).
+struct Plan {
+  Source src;
+  int64_t token_items;  // items of the token phase
+  int64_t check_items;  // tile validation items (kTileTable only)
+};
+
+Plan plan_tokens(int64_t has_segments, int64_t num_work_tiles, int64_t n_tokens) {
+  if (!has_segments) {
+    const int64_t covered = num_work_tiles * kTile;
+    return {Source::kDense, (covered < n_tokens ? covered : n_tokens) * kParts, 0};
+  }
+  if (num_work_tiles == 0 || n_tokens == 0) return {Source::kTileSlots, 0, 0};
+  if (num_work_tiles + 1 <= kTableCap) return {Source::kTileTable, n_tokens * kParts, num_work_tiles};
+  return {Source::kTileSlots, num_work_tiles * kTile * kParts, 0};
+}
+
+template <typename Kernel>
+int launch_plan(Kernel kernel, const Plan& plan, const RopeArgs& a, cudaStream_t stream, bool staged_table = true) {
+  const int64_t total = int64_t(a.q_items) + plan.token_items + plan.check_items;
+  if (plan.src == Source::kTileTable) {
+    const size_t smem = staged_table ? (size_t(a.num_tiles + 1) * sizeof(int32_t) + 15) & ~size_t(15) : 0;
+    return launch(kernel, unsigned((total + kBlock - 1) / kBlock), kBlock, smem, stream, a);
+  }
+  return launch(kernel, grid_for(total), kBlock, 0, stream, a);
+}
+
+}  // namespace
+
+#endif  // WELM_ROPE_HOST_CUH_

@@ -1,0 +1,317 @@
+// rope_mirror.cu — KV-mirror kernels (tile-table / slot / dense sources, and
+// the variant driven by request lengths) and their C entries.
+
+#include "rope_host.cuh"
+
+namespace {
+
+// ---------------------------------------------------------------------------
+// KV-mirror prefill.  Items [0, q_items) are the BS Q rows (6 heads at
+// positions[last_index[b]], bench_welmv4_inplace_rope_npu.py:839-854); the
+// next k_items are K tokens (1 head at positions[t],
+// bench_welmv4_inplace_rope_npu.py:856-919).  Q rows and K rows are disjoint
+// tensors, so the two phases need no ordering.  A Q row's data loads are
+// issued before its last_index -> position -> cache chain.
+// ---------------------------------------------------------------------------
+// g has been issued (with or without hints) before src is known.
+template <bool kVec>
+__device__ __forceinline__ void finish_q_row(const RopeArgs& a, Slices<kVec, kQHeads>& qx, int64_t src,
+                                             RowGather<kVec>& g, int part) {
+  if (src < 0 || src >= a.n_tokens) {
+    if (part == 0) raise_status(a.status, WELM_ROPE_DEV_BAD_LAST_INDEX);
+    return;
+  }
+  if (!g.finish(a, g.position(a, src), part)) {
+    if (part == 0) raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
+    return;
+  }
+  qx.rotate_store(g.cs);
+}
+
+template <bool kVec>
+__device__ __forceinline__ void mirror_q_row(const RopeArgs& a, int b, int part, int64_t src_hint,
+                                             int64_t pos_hint) {
+  Slices<kVec, kQHeads> qx;
+  qx.load(a.q + int64_t(b) * a.q_stride, part);
+  const int64_t src = __ldg(a.last_index + b);
+  RowGather<kVec> g;
+  g.issue(a, src_hint, pos_hint, part);
+  finish_q_row<kVec>(a, qx, src, g, part);
+}
+
+template <bool kVec>
+__device__ __forceinline__ void mirror_k_token(const RopeArgs& a, int64_t tok, int part, int64_t pos_hint) {
+  const int64_t pos = __ldg(a.positions + tok);
+  Slices<kVec, 1> kx;
+  kx.load(a.k + tok * a.k_stride, part);
+  RowGather<kVec> g;
+  g.issue(a, -1, pos_hint, part);
+  if (!g.finish(a, pos, part)) {
+    if (part == 0) raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
+    return;
+  }
+  kx.rotate_store(g.cs);
+}
+
+// At most 128 registers: 4 CTAs per SM keep a 16384-token launch in one wave.
+template <bool kVec, Source kSrc>
+__global__ void __launch_bounds__(kBlock, 4) rope_mirror_kernel(const RopeArgs a) {
+  // warm the first item's cos/sin row (Q rows: through a last_index hint)
+  const int item0 = blockIdx.x * blockDim.x + threadIdx.x;
+  int64_t src_hint = -1, pos_hint = -1;
+  if (kSrc == Source::kTileTable) prefetch_lines(a.tile_starts, int64_t(a.num_tiles + 1) * sizeof(int32_t));
+  if (item0 < a.q_items) {
+    src_hint = hint_load(a.last_index + (item0 >> kPartShift));
+    if (src_hint >= 0 && src_hint < a.n_tokens) pos_hint = hint_load(a.positions + src_hint);
+  } else if (kSrc != Source::kTileSlots && item0 - a.q_items < a.k_items) {
+    pos_hint = hint_load(a.positions + ((item0 - a.q_items) >> kPartShift));
+  }
+  prefetch_cos_sin_row(a.cache, a.max_position, pos_hint, item0 & (kParts - 1));
+  pdl_enter();
+  if constexpr (kSrc == Source::kTileTable) {
+    // One item per thread: Q rows, then tokens [0, k_items / 4), then one
+    // check per tile.  Phase 1 issues the loads of whatever item the thread
+    // owns; the coverage search (warp-uniform, no barrier) runs while they
+    // fly; phase 2 finishes the item.
+    const int item = blockIdx.x * blockDim.x + threadIdx.x;
+    const int part = item & (kParts - 1);
+    const bool is_q = item < a.q_items;
+    const int k_item = item - a.q_items;
+    const bool is_token = !is_q && k_item < a.k_items;
+    const int64_t tok = is_token ? (k_item >> kPartShift) : 0;
+    Slices<kVec, kQHeads> qx;
+    Slices<kVec, 1> kx;
+    RowGather<kVec> g;
+    int64_t src = 0, pos = 0;
+    if (is_q) {
+      qx.load(a.q + int64_t(item >> kPartShift) * a.q_stride, part);
+      src = __ldg(a.last_index + (item >> kPartShift));
+      g.issue(a, src_hint, pos_hint, part);
+    } else if (is_token) {
+      pos = __ldg(a.positions + tok);
+      kx.load(a.k + tok * a.k_stride, part);
+      g.issue(a, -1, pos_hint, part);
+    } else if (k_item - a.k_items < a.num_tiles) {
+      check_tile(a, k_item - a.k_items);
+    }
+    // the coverage search runs while the loads above are in flight
+    const int first_k = max(item & ~31, a.q_items) - a.q_items;  // the warp's first K item
+    const int64_t t_ref = first_k < a.k_items ? int64_t(first_k >> kPartShift) : 0;
+    const bool covered = warp_table_covers(a.tile_starts, a.num_tiles, t_ref, is_token ? tok : t_ref);
+    if (is_q) {
+      finish_q_row<kVec>(a, qx, src, g, part);
+    } else if (is_token && covered) {
+      if (g.finish(a, pos, part)) {
+        kx.rotate_store(g.cs);
+      } else if (part == 0) {
+        raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
+      }
+    }
+  } else {
+    const int stride = gridDim.x * blockDim.x;
+    const int total = a.q_items + a.k_items;
+    for (int item = blockIdx.x * blockDim.x + threadIdx.x; item < total; item += stride) {
+      const int part = item & (kParts - 1);
+      const bool first = item == item0;
+      if (item < a.q_items) {
+        mirror_q_row<kVec>(a, item >> kPartShift, part, first ? src_hint : -1, first ? pos_hint : -1);
+      } else {
+        int64_t tok;
+        if (slot_token<kSrc>(a, (item - a.q_items) >> kPartShift, part, tok))
+          mirror_k_token<kVec>(a, tok, part, first ? pos_hint : -1);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// KV mirror from request lengths.  Every CTA stages the BS lengths into shared
+// memory (cp.async) while its K-token loads and cache gathers fly; after the
+// one barrier each warp derives what it needs with shuffles, without further
+// CTA-wide synchronisation: K token t is rotated iff t < sum(lengths), Q row
+// r uses src = end_r - 1 with end_r = lengths[0] + ... + lengths[r].  One
+// item per thread: Q rows, then K tokens.
+// ---------------------------------------------------------------------------
+constexpr int kLensCap = WELM_ROPE_LENS_MAX_BATCH;
+
+// Warp-cooperative prefix over the staged lengths (negative entries count as
+// 0): returns the total and, for `row` in [0, n), end_row = s[0] + ... +
+// s[row].  Every lane of the warp must call it (it shuffles).
+__device__ __forceinline__ int64_t warp_request_ends(const int64_t* s, int n, int row, int64_t& end_row,
+                                                     bool& negative) {
+  const int lane = threadIdx.x & 31;
+  const int chunk = (n + 31) >> 5;
+  const int lo = min(n, lane * chunk), hi = min(n, lo + chunk);
+  int64_t part_sum = 0;
+  for (int i = lo; i < hi; ++i) {
+    const int64_t v = s[i];
+    negative |= v < 0;
+    part_sum += v > 0 ? v : 0;
+  }
+  negative = __any_sync(0xffffffffu, negative);
+  int64_t incl = part_sum;  // inclusive scan of the lanes' chunk sums
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int64_t t = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += t;
+  }
+  const int64_t total = __shfl_sync(0xffffffffu, incl, 31);
+  const int c = row >= 0 && row < n ? row / chunk : 0;  // the chunk holding `row`
+  const int64_t before = __shfl_sync(0xffffffffu, incl - part_sum, c);
+  end_row = before;
+  if (row >= 0 && row < n) {
+    for (int i = c * chunk; i <= row; ++i) {
+      const int64_t v = s[i];
+      end_row += v > 0 ? v : 0;
+    }
+  }
+  return total;
+}
+
+// At most 128 registers, so 4 CTAs fit per SM and a 16384-token launch
+// (516 CTAs) stays resident in one wave on 148 SMs.
+template <bool kVec>
+__global__ void __launch_bounds__(kBlock, 4) rope_mirror_lens_kernel(const RopeArgs a, const int64_t* lens, int batch) {
+  extern __shared__ int64_t s_len[];
+  // K tokens: warm the first item's cos/sin row; the lengths every CTA stages
+  int64_t pos_hint = -1;
+  prefetch_lines(lens, int64_t(batch) * sizeof(int64_t));
+  {
+    const int item0 = blockIdx.x * blockDim.x + threadIdx.x;
+    if (item0 >= a.q_items && item0 - a.q_items < a.k_items) {
+      pos_hint = hint_load(a.positions + ((item0 - a.q_items) >> kPartShift));
+      prefetch_cos_sin_row(a.cache, a.max_position, pos_hint, item0 & (kParts - 1));
+    }
+  }
+  pdl_enter();
+  for (int j = threadIdx.x; j < batch; j += blockDim.x) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(s_len + j)), "l"(lens + j) : "memory");
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  const int item = blockIdx.x * blockDim.x + threadIdx.x;
+  const int part = item & (kParts - 1);
+  const bool is_q = item < a.q_items;
+  const int k_item = item - a.q_items;
+  const bool is_token = !is_q && k_item < a.k_items;
+  const int64_t tok = is_token ? (k_item >> kPartShift) : 0;
+  Slices<kVec, kQHeads> qx;
+  Slices<kVec, 1> kx;
+  RowGather<kVec> g;
+  bool pos_ok = false;
+  if (is_q) {
+    qx.load(a.q + int64_t(item >> kPartShift) * a.q_stride, part);
+  } else if (is_token) {
+    const int64_t pos = __ldg(a.positions + tok);
+    kx.load(a.k + tok * a.k_stride, part);
+    g.issue(a, -1, pos_hint, part);
+    pos_ok = g.finish(a, pos, part);
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
+  int64_t end_row = 0;
+  bool negative = false;
+  const int64_t total = warp_request_ends(s_len, batch, is_q ? (item >> kPartShift) : -1, end_row, negative);
+  if (is_q) {
+    finish_q_row<kVec>(a, qx, end_row - 1, g, part);  // g was not issued: plain chain
+  } else if (is_token && tok < total) {
+    if (pos_ok) {
+      kx.rotate_store(g.cs);
+    } else if (part == 0) {
+      raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
+    }
+  }
+  if (negative && blockIdx.x == 0 && threadIdx.x == 0) raise_status(a.status, WELM_ROPE_DEV_BAD_LENGTH);
+}
+
+template <bool kVec>
+int launch_mirror(const Plan& plan, const RopeArgs& a, cudaStream_t s) {
+  switch (plan.src) {
+    case Source::kDense: return launch_plan(rope_mirror_kernel<kVec, Source::kDense>, plan, a, s);
+    case Source::kTileTable: return launch_plan(rope_mirror_kernel<kVec, Source::kTileTable>, plan, a, s, false);
+    default: return launch_plan(rope_mirror_kernel<kVec, Source::kTileSlots>, plan, a, s);
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int welm_rope_mirror(void* q, void* k, const int64_t* positions, const float* cos_sin_cache,
+                     const int64_t* last_index, const int32_t* segment_tile_starts,
+                     int64_t num_work_tiles, int64_t n_tokens, int64_t batch_size,
+                     int64_t q_token_stride, int64_t k_token_stride, int64_t has_segments,
+                     int64_t max_position, int32_t* device_status, void* stream) {
+  if (has_segments != 0 && has_segments != 1) return WELM_ROPE_ERR_BAD_MODE;
+  if (num_work_tiles < 0 || n_tokens < 0 || batch_size < 0 || max_position < 0)
+    return WELM_ROPE_ERR_BAD_SIZE;
+  if (num_work_tiles > kMaxItems / (kTile * kParts) || n_tokens > kMaxItems / kParts ||
+      batch_size > kMaxItems / kParts)
+    return WELM_ROPE_ERR_BAD_SIZE;
+  const Plan plan = n_tokens > 0 ? plan_tokens(has_segments, num_work_tiles, n_tokens) : Plan{Source::kDense, 0, 0};
+  const int64_t rows = n_tokens > 0 ? batch_size : 0;  // Q rows need a valid last_index target
+  if (rows * kParts + plan.token_items + plan.check_items > kMaxItems) return WELM_ROPE_ERR_BAD_SIZE;
+  if (plan.token_items == 0 && rows == 0) return WELM_ROPE_OK;
+  if (!positions || !cos_sin_cache) return WELM_ROPE_ERR_NULL_POINTER;
+  if (rows > 0 && (!q || !last_index)) return WELM_ROPE_ERR_NULL_POINTER;
+  if (plan.token_items > 0 && !k) return WELM_ROPE_ERR_NULL_POINTER;
+  if (has_segments && plan.token_items > 0 && !segment_tile_starts) return WELM_ROPE_ERR_NULL_POINTER;
+  if ((rows > 1 && q_token_stride < kQHeads * kHeadDim) || (n_tokens > 1 && k_token_stride < kHeadDim))
+    return WELM_ROPE_ERR_BAD_STRIDE;
+
+  RopeArgs a{};
+  a.q = static_cast<uint16_t*>(q);
+  a.k = static_cast<uint16_t*>(k);
+  a.positions = positions;
+  a.cache = cos_sin_cache;
+  a.last_index = last_index;
+  a.tile_starts = segment_tile_starts;
+  a.q_stride = q_token_stride;
+  a.k_stride = k_token_stride;
+  a.n_tokens = n_tokens;
+  a.max_position = max_position;
+  a.status = device_status;
+  a.q_items = int32_t(rows * kParts);
+  a.k_items = int32_t(plan.token_items);
+  a.num_tiles = int32_t(num_work_tiles);
+  const bool vec = aligned16(q) && aligned16(k) && aligned16(cos_sin_cache) &&
+                   (rows <= 1 || q_token_stride % 8 == 0) &&
+                   (n_tokens <= 1 || k_token_stride % 8 == 0);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return vec ? launch_mirror<true>(plan, a, s) : launch_mirror<false>(plan, a, s);
+}
+
+int welm_rope_mirror_from_lens(void* q, void* k, const int64_t* positions, const float* cos_sin_cache,
+                               const int64_t* seq_lens, int64_t n_tokens, int64_t batch_size,
+                               int64_t q_token_stride, int64_t k_token_stride, int64_t max_position,
+                               int32_t* device_status, void* stream) {
+  if (n_tokens < 0 || batch_size < 0 || max_position < 0) return WELM_ROPE_ERR_BAD_SIZE;
+  if (batch_size > kLensCap || n_tokens > kMaxItems / kParts - kLensCap) return WELM_ROPE_ERR_BAD_SIZE;
+  if (batch_size == 0 || n_tokens == 0) return WELM_ROPE_OK;  // no request, or no token to rotate
+  if (!q || !k || !positions || !cos_sin_cache || !seq_lens) return WELM_ROPE_ERR_NULL_POINTER;
+  if ((batch_size > 1 && q_token_stride < kQHeads * kHeadDim) || (n_tokens > 1 && k_token_stride < kHeadDim))
+    return WELM_ROPE_ERR_BAD_STRIDE;
+  if ((reinterpret_cast<uintptr_t>(seq_lens) & 7u) != 0) return WELM_ROPE_ERR_BAD_STRIDE;  // 8-byte cp.async
+  RopeArgs a{};
+  a.q = static_cast<uint16_t*>(q);
+  a.k = static_cast<uint16_t*>(k);
+  a.positions = positions;
+  a.cache = cos_sin_cache;
+  a.q_stride = q_token_stride;
+  a.k_stride = k_token_stride;
+  a.n_tokens = n_tokens;
+  a.max_position = max_position;
+  a.status = device_status;
+  a.q_items = int32_t(batch_size * kParts);
+  a.k_items = int32_t(n_tokens * kParts);
+  const bool vec = aligned16(q) && aligned16(k) && aligned16(cos_sin_cache) &&
+                   (batch_size <= 1 || q_token_stride % 8 == 0) && (n_tokens <= 1 || k_token_stride % 8 == 0);
+  const int64_t total = int64_t(a.q_items) + a.k_items;
+  const unsigned grid = unsigned((total + kBlock - 1) / kBlock);
+  const size_t smem = size_t(batch_size) * sizeof(int64_t);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int b = int(batch_size);
+  return vec ? launch(rope_mirror_lens_kernel<true>, grid, kBlock, smem, s, a, seq_lens, b)
+             : launch(rope_mirror_lens_kernel<false>, grid, kBlock, smem, s, a, seq_lens, b);
+}
+
+}  // extern "C"

@@ -1,0 +1,128 @@
+// rope_ordinary.cu — ordinary prefill / decode kernel (dense, staged tile
+// table and tile slots) and its C entry welm_rope_ordinary.
+
+#include "rope_host.cuh"
+
+namespace {
+
+// ---------------------------------------------------------------------------
+// Ordinary prefill / decode: K head + 6 Q heads of token t at positions[t];
+// the cache row is gathered once for all seven heads.
+// ---------------------------------------------------------------------------
+template <bool kVec>
+__device__ __forceinline__ void ordinary_token(const RopeArgs& a, int64_t tok, int part, int64_t pos_hint) {
+  const int64_t pos = __ldg(a.positions + tok);
+  Slices<kVec, 1> kx;
+  Slices<kVec, kQHeads> qx;
+  kx.load(a.k + tok * a.k_stride, part);
+  qx.load(a.q + tok * a.q_stride, part);
+  RowGather<kVec> g;
+  g.issue(a, -1, pos_hint, part);
+  if (!g.finish(a, pos, part)) {
+    if (part == 0) raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
+    return;
+  }
+  kx.rotate_store(g.cs);
+  qx.rotate_store(g.cs);
+}
+
+template <bool kVec, Source kSrc>
+__global__ void __launch_bounds__(kBlock) rope_ordinary_kernel(const RopeArgs a) {
+  extern __shared__ int32_t s_tab[];
+  const int item0 = blockIdx.x * blockDim.x + threadIdx.x;
+  int64_t pos_hint = -1;
+  if (kSrc == Source::kTileTable) prefetch_lines(a.tile_starts, int64_t(a.num_tiles + 1) * sizeof(int32_t));
+  if (kSrc != Source::kTileSlots && item0 < a.k_items) {  // tokens are items: warm the first item's row
+    pos_hint = hint_load(a.positions + (item0 >> kPartShift));
+    prefetch_cos_sin_row(a.cache, a.max_position, pos_hint, item0 & (kParts - 1));
+  }
+  pdl_enter();
+  if constexpr (kSrc == Source::kTileTable) {
+    // One item per thread: tokens [0, k_items / 4), then one check per tile.
+    stage_table_async(s_tab, a.tile_starts, a.num_tiles + 1);
+    const int item = blockIdx.x * blockDim.x + threadIdx.x;
+    const int part = item & (kParts - 1);
+    const bool is_token = item < a.k_items;
+    const int64_t tok = is_token ? (item >> kPartShift) : 0;
+    Slices<kVec, 1> kx;
+    Slices<kVec, kQHeads> qx;
+    RowGather<kVec> g;
+    bool pos_ok = false;
+    if (is_token) {
+      const int64_t pos = __ldg(a.positions + tok);
+      kx.load(a.k + tok * a.k_stride, part);
+      qx.load(a.q + tok * a.q_stride, part);
+      g.issue(a, -1, pos_hint, part);
+      pos_ok = g.finish(a, pos, part);
+    } else if (item - a.k_items < a.num_tiles) {
+      check_tile(a, item - a.k_items);
+    }
+    stage_table_wait();  // every thread of the CTA reaches this once
+    if (is_token && table_covers(s_tab, a.num_tiles, tok)) {
+      if (pos_ok) {
+        kx.rotate_store(g.cs);
+        qx.rotate_store(g.cs);
+      } else if (part == 0) {
+        raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
+      }
+    }
+  } else {
+    const int stride = gridDim.x * blockDim.x;
+    for (int item = blockIdx.x * blockDim.x + threadIdx.x; item < a.k_items; item += stride) {
+      const int part = item & (kParts - 1);
+      int64_t tok;
+      if (slot_token<kSrc>(a, item >> kPartShift, part, tok))
+        ordinary_token<kVec>(a, tok, part, item == item0 ? pos_hint : -1);
+    }
+  }
+}
+
+template <bool kVec>
+int launch_ordinary(const Plan& plan, const RopeArgs& a, cudaStream_t s) {
+  switch (plan.src) {
+    case Source::kDense: return launch_plan(rope_ordinary_kernel<kVec, Source::kDense>, plan, a, s);
+    case Source::kTileTable: return launch_plan(rope_ordinary_kernel<kVec, Source::kTileTable>, plan, a, s);
+    default: return launch_plan(rope_ordinary_kernel<kVec, Source::kTileSlots>, plan, a, s);
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int welm_rope_ordinary(void* q, void* k, const int64_t* positions, const float* cos_sin_cache,
+                       const int32_t* segment_tile_starts, int64_t num_work_tiles,
+                       int64_t n_tokens, int64_t q_token_stride, int64_t k_token_stride,
+                       int64_t has_segments, int64_t max_position, int32_t* device_status,
+                       void* stream) {
+  if (has_segments != 0 && has_segments != 1) return WELM_ROPE_ERR_BAD_MODE;
+  if (num_work_tiles < 0 || n_tokens < 0 || max_position < 0) return WELM_ROPE_ERR_BAD_SIZE;
+  if (num_work_tiles > kMaxItems / (kTile * kParts) || n_tokens > kMaxItems / kParts)
+    return WELM_ROPE_ERR_BAD_SIZE;
+  const Plan plan = plan_tokens(has_segments, num_work_tiles, n_tokens);
+  if (plan.token_items == 0) return WELM_ROPE_OK;  // nothing to rotate
+  if (!q || !k || !positions || !cos_sin_cache) return WELM_ROPE_ERR_NULL_POINTER;
+  if (has_segments && !segment_tile_starts) return WELM_ROPE_ERR_NULL_POINTER;
+  if (n_tokens > 1 && (q_token_stride < kQHeads * kHeadDim || k_token_stride < kHeadDim))
+    return WELM_ROPE_ERR_BAD_STRIDE;
+
+  RopeArgs a{};
+  a.q = static_cast<uint16_t*>(q);
+  a.k = static_cast<uint16_t*>(k);
+  a.positions = positions;
+  a.cache = cos_sin_cache;
+  a.tile_starts = segment_tile_starts;
+  a.q_stride = q_token_stride;
+  a.k_stride = k_token_stride;
+  a.n_tokens = n_tokens;
+  a.max_position = max_position;
+  a.status = device_status;
+  a.k_items = int32_t(plan.token_items);
+  a.num_tiles = int32_t(num_work_tiles);
+  const bool vec = aligned16(q) && aligned16(k) && aligned16(cos_sin_cache) &&
+                   (n_tokens <= 1 || (q_token_stride % 8 == 0 && k_token_stride % 8 == 0));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return vec ? launch_ordinary<true>(plan, a, s) : launch_ordinary<false>(plan, a, s);
+}
+
+}  // extern "C"
