@@ -137,14 +137,14 @@ constexpr int kLensCap = WELM_ROPE_LENS_MAX_BATCH;
 // Warp-cooperative prefix over the staged lengths (negative entries count as
 // 0): returns the total and, for `row` in [0, n), end_row = s[0] + ... +
 // s[row].  Every lane of the warp must call it (it shuffles).
-__device__ __forceinline__ int64_t warp_request_ends(const int64_t* s, int n, int row, int64_t& end_row,
-                                                     bool& negative) {
+template <typename Load>
+__device__ __forceinline__ int64_t warp_request_ends(Load load, int n, int row, int64_t& end_row, bool& negative) {
   const int lane = threadIdx.x & 31;
   const int chunk = (n + 31) >> 5;
   const int lo = min(n, lane * chunk), hi = min(n, lo + chunk);
   int64_t part_sum = 0;
   for (int i = lo; i < hi; ++i) {
-    const int64_t v = s[i];
+    const int64_t v = load(i);
     negative |= v < 0;
     part_sum += v > 0 ? v : 0;
   }
@@ -161,7 +161,7 @@ __device__ __forceinline__ int64_t warp_request_ends(const int64_t* s, int n, in
   end_row = before;
   if (row >= 0 && row < n) {
     for (int i = c * chunk; i <= row; ++i) {
-      const int64_t v = s[i];
+      const int64_t v = load(i);
       end_row += v > 0 ? v : 0;
     }
   }
@@ -173,15 +173,26 @@ __device__ __forceinline__ int64_t warp_request_ends(const int64_t* s, int n, in
 template <bool kVec>
 __global__ void __launch_bounds__(kBlock, 4) rope_mirror_lens_kernel(const RopeArgs a, const int64_t* lens, int batch) {
   extern __shared__ int64_t s_len[];
-  // K tokens: warm the first item's cos/sin row; the lengths every CTA stages
-  int64_t pos_hint = -1;
+  // Before the wait: K tokens warm their cos/sin row; warps holding Q rows
+  // scan hint copies of the lengths for each row's source token and warm
+  // that token's row (the real scan after the barrier confirms the hints).
+  int64_t src_hint = -1, pos_hint = -1;
   prefetch_lines(lens, int64_t(batch) * sizeof(int64_t));
   {
     const int item0 = blockIdx.x * blockDim.x + threadIdx.x;
-    if (item0 >= a.q_items && item0 - a.q_items < a.k_items) {
-      pos_hint = hint_load(a.positions + ((item0 - a.q_items) >> kPartShift));
-      prefetch_cos_sin_row(a.cache, a.max_position, pos_hint, item0 & (kParts - 1));
+    if ((item0 & ~31) < a.q_items) {  // warp-uniform: the scan shuffles
+      int64_t end_hint = 0;
+      bool neg_hint = false;
+      warp_request_ends([&](int i) { return hint_load(lens + i); }, batch,
+                        item0 < a.q_items ? (item0 >> kPartShift) : -1, end_hint, neg_hint);
+      if (item0 < a.q_items) {
+        src_hint = end_hint - 1;
+        if (src_hint >= 0 && src_hint < a.n_tokens) pos_hint = hint_load(a.positions + src_hint);
+      }
     }
+    if (item0 >= a.q_items && item0 - a.q_items < a.k_items)
+      pos_hint = hint_load(a.positions + ((item0 - a.q_items) >> kPartShift));
+    prefetch_cos_sin_row(a.cache, a.max_position, pos_hint, item0 & (kParts - 1));
   }
   pdl_enter();
   for (int j = threadIdx.x; j < batch; j += blockDim.x) {
@@ -200,6 +211,7 @@ __global__ void __launch_bounds__(kBlock, 4) rope_mirror_lens_kernel(const RopeA
   bool pos_ok = false;
   if (is_q) {
     qx.load(a.q + int64_t(item >> kPartShift) * a.q_stride, part);
+    g.issue(a, src_hint, pos_hint, part);
   } else if (is_token) {
     const int64_t pos = __ldg(a.positions + tok);
     kx.load(a.k + tok * a.k_stride, part);
@@ -210,9 +222,10 @@ __global__ void __launch_bounds__(kBlock, 4) rope_mirror_lens_kernel(const RopeA
   __syncthreads();
   int64_t end_row = 0;
   bool negative = false;
-  const int64_t total = warp_request_ends(s_len, batch, is_q ? (item >> kPartShift) : -1, end_row, negative);
+  const int64_t total = warp_request_ends([&](int i) { return s_len[i]; }, batch,
+                                          is_q ? (item >> kPartShift) : -1, end_row, negative);
   if (is_q) {
-    finish_q_row<kVec>(a, qx, end_row - 1, g, part);  // g was not issued: plain chain
+    finish_q_row<kVec>(a, qx, end_row - 1, g, part);  // keeps the speculative loads only if the hints held
   } else if (is_token && tok < total) {
     if (pos_ok) {
       kx.rotate_store(g.cs);
