@@ -25,5 +25,6 @@ from .ops import (  # noqa: F401
     welmv4_inplace_rope_npu,
 )
 from .host import welmv4_inplace_rope_host  # noqa: F401,E402
+from .harness import Harness, providers_for_case  # noqa: F401,E402
 
 __version__ = "0.1.0"

@@ -77,8 +77,20 @@ class Case:
         return self.phase.startswith("prefill_mirror")
 
     @property
+    def is_contiguous_mirror(self) -> bool:
+        return self.phase == "prefill_mirror_contiguous"
+
+    @property
+    def is_segmented_mirror(self) -> bool:
+        return self.phase == "prefill_mirror_segmented"
+
+    @property
     def is_segmented(self) -> bool:
         return bool(self.segment_lens)
+
+    @property
+    def request_count(self) -> int:
+        return len(self.segment_lens)
 
     @property
     def q_rows(self) -> int:
