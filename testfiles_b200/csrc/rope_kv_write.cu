@@ -38,16 +38,16 @@ struct HeadPiece {
   uint4 nope[kNopeChunks];
   uint4 x1, x2;
   __device__ __forceinline__ void load(const uint16_t* head, int part) {
-    const uint16_t* n = head + part * (kNope / kParts);
+    const uint16_t* n = head + part * 8;
 #pragma unroll
-    for (int c = 0; c < kNopeChunks; ++c) nope[c] = *reinterpret_cast<const uint4*>(n + 8 * c);
+    for (int c = 0; c < kNopeChunks; ++c) nope[c] = *reinterpret_cast<const uint4*>(n + 8 * kParts * c);
     x1 = *reinterpret_cast<const uint4*>(head + kRopeLane0 + part * kLanes);
     x2 = *reinterpret_cast<const uint4*>(head + kRopeLane0 + kHalf + part * kLanes);
   }
   __device__ __forceinline__ void store(uint16_t* head, int part) const {
-    uint16_t* n = head + part * (kNope / kParts);
+    uint16_t* n = head + part * 8;
 #pragma unroll
-    for (int c = 0; c < kNopeChunks; ++c) *reinterpret_cast<uint4*>(n + 8 * c) = nope[c];
+    for (int c = 0; c < kNopeChunks; ++c) *reinterpret_cast<uint4*>(n + 8 * kParts * c) = nope[c];
     *reinterpret_cast<uint4*>(head + kRopeLane0 + part * kLanes) = x1;
     *reinterpret_cast<uint4*>(head + kRopeLane0 + kHalf + part * kLanes) = x2;
   }
@@ -99,9 +99,9 @@ __global__ void __launch_bounds__(kBlock) rope_mirror_kv_write_kernel(const KvAr
       uint4 vv[kVChunks];
       const bool with_v = a.v != nullptr && a.value_cache != nullptr;
       if (with_v) {
-        const uint16_t* vsrc = a.v + tok * a.v_stride + part * (kHeadDim / kParts);
+        const uint16_t* vsrc = a.v + tok * a.v_stride + part * 8;
 #pragma unroll
-        for (int c = 0; c < kVChunks; ++c) vv[c] = *reinterpret_cast<const uint4*>(vsrc + 8 * c);
+        for (int c = 0; c < kVChunks; ++c) vv[c] = *reinterpret_cast<const uint4*>(vsrc + 8 * kParts * c);
       }
       if (pos < 0 || pos >= a.max_position) {
         if (part == 0 && slot >= 0) raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
@@ -117,9 +117,9 @@ __global__ void __launch_bounds__(kBlock) rope_mirror_kv_write_kernel(const KvAr
       rotate8(kp.x1, kp.x2, cs);
       kp.store(a.key_cache + slot * a.slot_stride, part);
       if (with_v) {
-        uint16_t* vdst = a.value_cache + slot * a.slot_stride + part * (kHeadDim / kParts);
+        uint16_t* vdst = a.value_cache + slot * a.slot_stride + part * 8;
 #pragma unroll
-        for (int c = 0; c < kVChunks; ++c) *reinterpret_cast<uint4*>(vdst + 8 * c) = vv[c];
+        for (int c = 0; c < kVChunks; ++c) *reinterpret_cast<uint4*>(vdst + 8 * kParts * c) = vv[c];
       }
     }
   }
