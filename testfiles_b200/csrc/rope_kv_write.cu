@@ -54,16 +54,19 @@ struct HeadPiece {
 };
 
 __global__ void __launch_bounds__(kBlock) rope_mirror_kv_write_kernel(const KvArgs a) {
-  {  // warm the first item's cos/sin row (Q rows: through a last_index hint)
-    const int item0 = blockIdx.x * blockDim.x + threadIdx.x;
+  // warm the first item's cos/sin row (Q rows: through a last_index hint);
+  // a K token also keeps its position hint for the speculative gather below
+  const int item0 = blockIdx.x * blockDim.x + threadIdx.x;
+  int64_t pos_hint = -1;
+  {
     const int part0 = item0 & (kParts - 1);
     if (item0 < a.q_items) {
       const int64_t src = hint_load(a.last_index + item0 / (kQHeads * kParts));
       if (src >= 0 && src < a.n_tokens)
         prefetch_cos_sin_row(a.cache, a.max_position, hint_load(a.positions + src), part0);
     } else if (item0 - a.q_items < a.k_items) {
-      prefetch_cos_sin_row(a.cache, a.max_position, hint_load(a.positions + ((item0 - a.q_items) >> kPartShift)),
-                           part0);
+      pos_hint = hint_load(a.positions + ((item0 - a.q_items) >> kPartShift));
+      prefetch_cos_sin_row(a.cache, a.max_position, pos_hint, part0);
     }
   }
   pdl_enter();
@@ -92,6 +95,19 @@ __global__ void __launch_bounds__(kBlock) rope_mirror_kv_write_kernel(const KvAr
       piece.store(a.q_out + int64_t(b) * a.q_out_stride + h * kHeadDim, part);
     } else {
       const int64_t tok = (item - a.q_items) >> kPartShift;
+      // speculative cos/sin at the position hint, issued with the real loads
+      CosSin cs;
+      const bool spec = item == item0 && pos_hint >= 0 && pos_hint < a.max_position;
+      if (spec) {
+        const float* row = a.cache + pos_hint * kRopeDim;
+        const float4 c0 = pinned_load_f4(row + part * kLanes), c1 = pinned_load_f4(row + part * kLanes + 4);
+        const float4 s0 = pinned_load_f4(row + kHalf + part * kLanes);
+        const float4 s1 = pinned_load_f4(row + kHalf + part * kLanes + 4);
+        cs.c[0] = c0.x; cs.c[1] = c0.y; cs.c[2] = c0.z; cs.c[3] = c0.w;
+        cs.c[4] = c1.x; cs.c[5] = c1.y; cs.c[6] = c1.z; cs.c[7] = c1.w;
+        cs.s[0] = s0.x; cs.s[1] = s0.y; cs.s[2] = s0.z; cs.s[3] = s0.w;
+        cs.s[4] = s1.x; cs.s[5] = s1.y; cs.s[6] = s1.z; cs.s[7] = s1.w;
+      }
       const int64_t slot = __ldg(a.slots + tok);
       const int64_t pos = __ldg(a.positions + tok);
       HeadPiece kp;
@@ -107,8 +123,7 @@ __global__ void __launch_bounds__(kBlock) rope_mirror_kv_write_kernel(const KvAr
         if (part == 0 && slot >= 0) raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
         continue;
       }
-      CosSin cs;
-      Io<true>::load_cos_sin(a.cache + pos * kRopeDim, part, cs);
+      if (!(spec && pos == pos_hint)) Io<true>::load_cos_sin(a.cache + pos * kRopeDim, part, cs);
       if (slot < 0) continue;  // padding token
       if (slot >= a.num_slots) {
         if (part == 0) raise_status(a.status, WELM_ROPE_DEV_BAD_SLOT);

@@ -88,3 +88,40 @@ def test_kv_write_without_v_and_bad_slots():
     assert status.item() == _native.DEV_BAD_SLOT
     assert torch.equal(q_out.cpu().view(torch.int16), want_q.view(torch.int16))
     assert torch.equal(ck.cpu().view(torch.int16), want_k.view(torch.int16))
+
+
+def test_kv_write_graph_replays_with_changing_positions():
+    """The producer (a copy of new positions and activations) and the fused
+    write in one CUDA graph: each replay's pre-wait position hints are stale
+    on purpose, and every replay must still equal the oracle."""
+    n, bs = 3000, 7
+    qkv, positions, last_index, slots, cache_k, cache_v, cos_sin = make_case(n, bs, 60, 64, 5)
+    qkv_src, pos_src = qkv.to(DEV), positions.to(DEV)
+    d, pos = torch.empty_like(qkv_src), torch.empty_like(pos_src)
+    q_out = torch.zeros((bs, 6, 256), dtype=torch.bfloat16, device=DEV)
+    ck, cv = cache_k.to(DEV), cache_v.to(DEV)
+    dev_cache, dev_last, dev_slots = cos_sin.to(DEV), last_index.to(DEV), slots.to(DEV)
+
+    def step():
+        d.copy_(qkv_src)
+        pos.copy_(pos_src)
+        welm.rope_mirror_kv_write(d[:, :1536].view(n, 6, 256), q_out, d[:, 1536:1792].view(n, 1, 256),
+                                  d[:, 1792:].view(n, 1, 256), pos, dev_cache, dev_last, dev_slots, ck, cv)
+
+    step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for seed in (1, 2, 3):
+        g = torch.Generator().manual_seed(seed)
+        new_pos = torch.randint(0, 4096, (n,), generator=g, dtype=torch.int64)
+        new_qkv = torch.randn((n, 8 * 256), generator=g).to(torch.bfloat16)
+        pos_src.copy_(new_pos)
+        qkv_src.copy_(new_qkv)
+        graph.replay()
+        torch.cuda.synchronize()
+        want_q, want_k, want_v = expected(new_qkv, new_pos, last_index, slots, cache_k, cache_v, cos_sin)
+        assert torch.equal(q_out.cpu().view(torch.int16), want_q.view(torch.int16)), seed
+        assert torch.equal(ck.cpu().view(torch.int16), want_k.view(torch.int16)), seed
+        assert torch.equal(cv.cpu().view(torch.int16), want_v.view(torch.int16)), seed
