@@ -25,6 +25,8 @@ pipeline-fill costs weigh as much as bandwidth.
 ``--host mapped|staged`` times the host-memory entry instead (ordinary
 cases): Q, K and positions in pinned host memory, every PCIe transfer inside
 the timed region, µs per call and GB/s each way over the bus.
+``--kv-write N,BS`` times the fused KV-mirror cache write (with ``--time``;
+with ``--iters`` it only launches it, for ncu).
 """
 
 from __future__ import annotations
@@ -244,6 +246,67 @@ def time_host_case(case: workloads.Case, device: torch.device, transport: str, t
     }
 
 
+def kv_write_bytes(n_tokens: int, batch: int) -> int:
+    """Algorithmic bytes of one fused KV-mirror write: per token K and V read
+    and written to the cache (4 x 512), position and slot (16), cos/sin row
+    (256); per request the Q row read and written (2 x 3072) and last_index."""
+    return 2320 * n_tokens + 6152 * batch
+
+
+def time_kv_write(n_tokens: int, batch: int, device: torch.device, trials: int = 7, graph_launches: int = 64,
+                  replays: int = 20, sets: int = 16, iters: int = 0) -> dict:
+    """µs per launch of rope_mirror_kv_write on a fused QKV projection output
+    [N, 8, 256] with seeded-uneven requests (positions restarting per
+    request), random slots of a [300, 64, 1, 256] paged cache, graph-replayed
+    over ``sets`` rotating buffer sets, with a same-size copy beside it.
+    ``iters`` > 0 only launches that many times (for ncu captures)."""
+    lens = workloads.seeded_uneven_lens(n_tokens, batch, 1)
+    last = (torch.tensor(lens).cumsum(0) - 1).to(device)
+    cache = workloads.make_cos_sin_cache(16384, 10000.0, device=device)
+    blocks = max(1, -(-n_tokens // 64) + 44)
+    g = torch.Generator(device=device).manual_seed(0)
+    bufs = []
+    for _ in range(1 if iters else sets):
+        qkv = torch.randn((n_tokens, 8 * 256), generator=g, device=device).to(torch.bfloat16)
+        pos = torch.cat([torch.arange(x) for x in lens]).to(device)
+        slots = torch.randperm(blocks * 64, generator=g, device=device)[:n_tokens]
+        ck = torch.zeros((blocks, 64, 1, 256), dtype=torch.bfloat16, device=device)
+        bufs.append((qkv, pos, slots, ck, torch.zeros_like(ck), torch.empty((batch, 6, 256), dtype=torch.bfloat16,
+                                                                              device=device), cache.clone()))
+
+    def call(i: int) -> None:
+        qkv, pos, slots, ck, cv, q_out, cs = bufs[i % len(bufs)]
+        ops.rope_mirror_kv_write(qkv[:, :1536].view(n_tokens, 6, 256), q_out, qkv[:, 1536:1792].view(n_tokens, 1, 256),
+                                 qkv[:, 1792:].view(n_tokens, 1, 256), pos, cs, last, slots, ck, cv)
+
+    if iters:
+        for i in range(iters):
+            call(i)
+        torch.cuda.synchronize(device)
+        return {"record_type": "launch", "kernel_name": "rope_mirror_kv_write_kernel", "n_tokens": n_tokens,
+                "batch_size": batch, "iters": iters}
+    for i in range(3):
+        call(i)
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(graph_launches):
+            call(i)
+    us = _replay_us(graph, device, trials, replays, graph_launches)
+    del graph
+    nbytes = kv_write_bytes(n_tokens, batch)
+    copy_us = same_size_copy_us(nbytes, sets, device, 5, graph_launches, replays)
+    peak, kind = measured_hbm_peak()
+    return {
+        "record_type": "timing", "case": f"kv_write_n{n_tokens}_bs{batch}", "path": "kv_mirror_write",
+        "n_tokens": n_tokens, "batch_size": batch, "us_per_launch": round(us, 3), "bytes_per_launch": nbytes,
+        "gb_s": round(nbytes / (us * 1e3), 1), "hbm_frac": round(nbytes / (us * 1e3) / peak, 4),
+        "hbm_peak_gbs": peak, "hbm_peak_source": kind, "same_size_copy_us": round(copy_us, 3),
+        "frac_of_same_size_copy": round(copy_us / us, 4), "buffer_sets": sets,
+        "device_name": torch.cuda.get_device_name(device),
+    }
+
+
 def launch_case(case: workloads.Case, device: torch.device, iters: int, from_lens: bool = False) -> dict:
     inp = workloads.make_inputs(case, device)
     if from_lens:
@@ -294,12 +357,23 @@ def main(argv: Optional[list[str]] = None) -> int:
                         help="with --time: also time a same-size device copy (the practical ceiling)")
     parser.add_argument("--host", choices=("mapped", "staged"), default=None,
                         help="time the host-memory entry on pinned Q/K with this transport (ordinary cases)")
+    parser.add_argument("--kv-write", default=None, metavar="N,BS",
+                        help="time the fused KV-mirror cache write for N tokens in BS requests (with --iters: "
+                             "only launch it)")
     args = parser.parse_args(argv)
     if not torch.cuda.is_available():
         print("the launcher needs a CUDA device", file=sys.stderr)
         return 2
     device = torch.device(args.device)
     torch.cuda.set_device(device)
+    if args.kv_write:
+        n, bs = (int(x) for x in args.kv_write.split(","))
+        rec = time_kv_write(n, bs, device, iters=0 if args.time else args.iters)
+        print(json.dumps(rec), flush=True)
+        if args.json:
+            with open(args.json, "a") as fh:
+                fh.write(json.dumps(rec) + "\n")
+        return 0
     run(select_cases(args.cases), device, args.time, args.iters, args.json, args.mirror_from_lens,
         args.copy_ceiling, args.host)
     return 0

@@ -42,3 +42,10 @@ def test_time_host_case(transport):
     assert rec["us_per_call"] > 0 and rec["d2h_bytes_per_call"] == 577 * 7 * 128
     with pytest.raises(ValueError):
         launcher.time_host_case(workloads.find_case("b_mirror_contiguous_n8192"), DEV, transport)
+
+
+def test_time_kv_write_record():
+    rec = launcher.time_kv_write(1000, 7, DEV, trials=2, graph_launches=4, replays=3, sets=2)
+    assert rec["us_per_launch"] > 0 and rec["bytes_per_launch"] == launcher.kv_write_bytes(1000, 7)
+    assert rec["same_size_copy_us"] > 0
+    assert launcher.time_kv_write(500, 3, DEV, iters=2)["record_type"] == "launch"
