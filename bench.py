@@ -27,8 +27,9 @@ cos/sin cache [16384, 64] (rotary base 1e4), seeded N(0,1) synthetic data.
   oracle port of its torch path) on this host's cores, same workload.
 * ``other_configs`` (rank 0, N=1 only): one configuration of each other
   judged family (prefill M=8192, decode M=1 and M=128, contiguous and
-  segmented KV mirror at N=16384) timed after the headline, with a same-size
-  device copy beside each (``--no-config-sweep`` skips it).
+  segmented KV mirror at N=16384) and the KV mirror fused with the paged
+  KV-cache write (N=16384, BS=128), timed after the headline, with a
+  same-size device copy beside each (``--no-config-sweep`` skips it).
 
 ``--impl reference`` times the reference's CPU implementation alone (rank 0;
 other ranks exit 0).  Multi-GPU runs (torchrun) shard requests: each rank
@@ -309,11 +310,19 @@ def other_config_records(device) -> list[dict]:
 
     keep = ("case", "phase", "n_tokens", "batch_size", "us_per_launch", "gb_s", "hbm_frac", "same_size_copy_us",
             "frac_of_same_size_copy", "l2_cold")
-    launcher.time_case(workloads.find_case(OTHER_CONFIGS[0]), device, trials=1)  # warm-up, discarded
+    # each configuration is timed twice and the faster record kept: the first
+    # timing after the headline's legs can read high
+    def best(timer):
+        a, b = timer(), timer()
+        return a if a["us_per_launch"] <= b["us_per_launch"] else b
+
     out = []
     for name in OTHER_CONFIGS:
-        rec = launcher.time_case(workloads.find_case(name), device, copy_ceiling=True)
+        rec = best(lambda: launcher.time_case(workloads.find_case(name), device, copy_ceiling=True))
         out.append({k: rec[k] for k in keep})
+    # the KV mirror fused with the paged KV-cache write (random slots)
+    rec = best(lambda: launcher.time_kv_write(16384, 128, device))
+    out.append({k: rec.get(k) for k in keep})
     return out
 
 
@@ -437,6 +446,10 @@ def run_b200_arm(args) -> int:
         del copy_graph, pairs
     torch.cuda.synchronize(device)
     del body, tail
+    # the timed legs are done: release their device buffers before the
+    # configuration sweep allocates its own
+    del sets, d_q, d_k, d_p
+    torch.cuda.empty_cache()
 
     per_step_s = elapsed_ms / 1e3 / args.steps
     total_bytes = algorithmic_bytes(TOKENS) * world

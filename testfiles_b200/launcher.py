@@ -298,12 +298,12 @@ def time_kv_write(n_tokens: int, batch: int, device: torch.device, trials: int =
     copy_us = same_size_copy_us(nbytes, sets, device, 5, graph_launches, replays)
     peak, kind = measured_hbm_peak()
     return {
-        "record_type": "timing", "case": f"kv_write_n{n_tokens}_bs{batch}", "path": "kv_mirror_write",
-        "n_tokens": n_tokens, "batch_size": batch, "us_per_launch": round(us, 3), "bytes_per_launch": nbytes,
+        "record_type": "timing", "case": f"kv_write_n{n_tokens}_bs{batch}", "phase": "prefill_mirror_kv_write",
+        "path": "kv_mirror_write", "n_tokens": n_tokens, "batch_size": batch, "us_per_launch": round(us, 3), "bytes_per_launch": nbytes,
         "gb_s": round(nbytes / (us * 1e3), 1), "hbm_frac": round(nbytes / (us * 1e3) / peak, 4),
         "hbm_peak_gbs": peak, "hbm_peak_source": kind, "same_size_copy_us": round(copy_us, 3),
         "frac_of_same_size_copy": round(copy_us / us, 4), "buffer_sets": sets,
-        "device_name": torch.cuda.get_device_name(device),
+        "l2_cold": sets * nbytes > 2 * L2_BYTES, "device_name": torch.cuda.get_device_name(device),
     }
 
 
