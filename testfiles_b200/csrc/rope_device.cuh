@@ -309,7 +309,7 @@ struct RowGather {
 // ---------------------------------------------------------------------------
 enum class Source { kDense, kTileTable, kTileSlots };
 
-constexpr int kTableCap = 2048;  // staged table entries (8 KB of shared memory)
+constexpr int kTableCap = 2048;  // table entries of the kTileTable source (8 KB when staged in shared memory)
 // warp_table_covers searches two levels of at most 32 x 64 entries
 static_assert(kTableCap <= 32 * 64, "the warp search covers at most 2048 table entries");
 

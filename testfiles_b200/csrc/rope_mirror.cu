@@ -129,7 +129,10 @@ __global__ void __launch_bounds__(kBlock, 4) rope_mirror_kernel(const RopeArgs a
 // memory (cp.async) while its K-token loads and cache gathers fly; after the
 // one barrier each warp derives what it needs with shuffles, without further
 // CTA-wide synchronisation: K token t is rotated iff t < sum(lengths), Q row
-// r uses src = end_r - 1 with end_r = lengths[0] + ... + lengths[r].  One
+// r uses src = end_r - 1 with end_r = lengths[0] + ... + lengths[r].  Before
+// the dependency wait, warps holding Q rows run the same scan over hint
+// copies of the lengths so each row's source position and cos/sin row can be
+// loaded speculatively; the real scan keeps them only if the hints held.  One
 // item per thread: Q rows, then K tokens.
 // ---------------------------------------------------------------------------
 constexpr int kLensCap = WELM_ROPE_LENS_MAX_BATCH;
