@@ -17,7 +17,9 @@ record states), CUDA events on the launching stream, median of 5 trials.
 Each record is one JSON line whose fields follow the reference's CSV record
 (bench_welmv4_inplace_rope_npu.py:1143-1162,1529-1540): ``record_type``,
 case fields, then µs per launch, tokens/s, GB/s of algorithmic bytes and the
-fraction of the HBM peak.  ``--copy-ceiling`` adds the time of a plain device
+fraction of the HBM peak, plus the SM clock and throttle reasons sampled
+during the timed replays; ``--csv`` writes the records as one table.
+``--copy-ceiling`` adds the time of a plain device
 copy moving the same bytes (half read, half written), replayed and rotated
 exactly like the op: the practical ceiling at that size, where launch and
 pipeline-fill costs weigh as much as bandwidth.
@@ -42,6 +44,7 @@ from typing import Iterable, Optional
 import torch
 
 from . import ops, workloads
+from .clocks import ClockSampler
 
 L2_BYTES = 126 * 1024 * 1024
 SPEC_HBM_GBS = 8000.0
@@ -174,7 +177,8 @@ def time_case(case: workloads.Case, device: torch.device, trials: int = 5, graph
     if replays is None:  # about 5 ms of launches per trial
         est_us = 1.5 + nbytes / 5e6
         replays = max(5, min(200, int(5e3 / (est_us * graph_launches))))
-    us = _replay_us(graph, device, trials, replays, graph_launches)
+    with ClockSampler(device.index) as clocks:
+        us = _replay_us(graph, device, trials, replays, graph_launches)
     del graph, buffers
     peak, kind = measured_hbm_peak()
     gbs = nbytes / (us * 1e3)
@@ -194,6 +198,7 @@ def time_case(case: workloads.Case, device: torch.device, trials: int = 5, graph
         "hbm_peak_source": kind,
         "hbm_frac_of_8tbs_spec": round(gbs / SPEC_HBM_GBS, 4),
         **ceiling,
+        "clocks": clocks.summary(),
         "buffer_sets": sets,
         "l2_cold": bool(sets * nbytes > 2 * L2_BYTES),
         "pdl": os.environ.get("WELM_ROPE_PDL", "1") != "0",
@@ -318,6 +323,22 @@ def launch_case(case: workloads.Case, device: torch.device, iters: int, from_len
             "kernel_name": "rope_mirror_kernel" if case.is_mirror else "rope_ordinary_kernel"}
 
 
+def write_csv(records: list[dict], path: str) -> None:
+    """Records as one CSV table over the union of their fields, in first-seen
+    order (the reference writes its records this way,
+    bench_welmv4_inplace_rope_npu.py:2178-2188); nested fields are JSON."""
+    import csv
+
+    fields: list[str] = []
+    for rec in records:
+        fields.extend(k for k in rec if k not in fields)
+    with open(path, "w", newline="") as fh:
+        writer = csv.DictWriter(fh, fieldnames=fields)
+        writer.writeheader()
+        for rec in records:
+            writer.writerow({k: json.dumps(v) if isinstance(v, (dict, list)) else v for k, v in rec.items()})
+
+
 def run(cases: Iterable[workloads.Case], device: torch.device, time_it: bool, iters: int,
         out: Optional[str], from_lens: bool = False, copy_ceiling: bool = False,
         host_transport: Optional[str] = None) -> list[dict]:
@@ -351,6 +372,7 @@ def main(argv: Optional[list[str]] = None) -> int:
     parser.add_argument("--iters", type=int, default=20, help="eager launches per case (without --time)")
     parser.add_argument("--device", default="cuda:0")
     parser.add_argument("--json", default=None, help="append JSON lines here")
+    parser.add_argument("--csv", default=None, help="write all records as one CSV table here")
     parser.add_argument("--mirror-from-lens", action="store_true",
                         help="run segmented KV-mirror cases through rope_mirror_from_lens")
     parser.add_argument("--copy-ceiling", action="store_true",
@@ -374,8 +396,10 @@ def main(argv: Optional[list[str]] = None) -> int:
             with open(args.json, "a") as fh:
                 fh.write(json.dumps(rec) + "\n")
         return 0
-    run(select_cases(args.cases), device, args.time, args.iters, args.json, args.mirror_from_lens,
-        args.copy_ceiling, args.host)
+    records = run(select_cases(args.cases), device, args.time, args.iters, args.json, args.mirror_from_lens,
+                  args.copy_ceiling, args.host)
+    if args.csv:
+        write_csv(records, args.csv)
     return 0
 
 

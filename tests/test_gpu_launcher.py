@@ -24,6 +24,7 @@ def test_time_case_with_copy_ceiling(name):
     assert rec["bytes_per_launch"] == workloads.min_bytes(case)
     assert 0 < rec["frac_of_same_size_copy"] < 10
     assert rec["gb_s"] == pytest.approx(rec["bytes_per_launch"] / (rec["us_per_launch"] * 1e3), rel=0.01)
+    assert set(rec["clocks"]) >= {"sm_mhz", "sm_max_mhz", "reasons", "samples"}
     json.dumps(rec)
 
 

@@ -255,3 +255,27 @@ def test_host_entry_transport_argument():
     pos = torch.zeros(2, dtype=torch.int64)
     with pytest.raises(ValueError, match="transport"):
         host.welmv4_inplace_rope_host(q, k, pos, torch.zeros((8, 64)), transport="zero-copy")
+
+
+def test_launcher_csv_writer(tmp_path):
+    import csv
+
+    from testfiles_b200 import launcher
+
+    recs = [{"record_type": "timing", "case": "a", "us_per_launch": 1.5, "clocks": {"sm_mhz": 1965}},
+            {"record_type": "launch", "case": "b", "iters": 3}]
+    path = tmp_path / "records.csv"
+    launcher.write_csv(recs, str(path))
+    rows = list(csv.DictReader(path.open()))
+    assert [r["case"] for r in rows] == ["a", "b"]
+    assert list(rows[0]) == ["record_type", "case", "us_per_launch", "clocks", "iters"]
+    assert rows[0]["clocks"] == '{"sm_mhz": 1965}' and rows[1]["us_per_launch"] == ""
+
+
+def test_clock_sampler_without_a_device_reports_no_samples():
+    from testfiles_b200.clocks import ClockSampler
+
+    with ClockSampler(0) as s:
+        pass
+    summary = s.summary()
+    assert summary["samples"] == 0 or summary["sm_mhz"] is not None
