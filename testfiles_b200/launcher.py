@@ -151,9 +151,12 @@ def same_size_copy_us(nbytes: int, sets: int, device: torch.device, trials: int 
 
 
 def time_case(case: workloads.Case, device: torch.device, trials: int = 5, graph_launches: int = 64,
-              replays: Optional[int] = None, from_lens: bool = False, copy_ceiling: bool = False) -> dict:
+              replays: Optional[int] = None, from_lens: bool = False, copy_ceiling: bool = False,
+              shared_cache: bool = False) -> dict:
     """µs per launch of ``case`` (graph-replayed over rotating buffer sets);
-    ``from_lens`` runs segmented mirror cases through rope_mirror_from_lens."""
+    ``from_lens`` runs segmented mirror cases through rope_mirror_from_lens.
+    ``shared_cache`` gives every set the same cos/sin cache (hot in L2, as
+    in serving) instead of a private copy each."""
     host = workloads.make_inputs(case, "cpu")
     nbytes = workloads.min_bytes(case)
     sets_needed = max(2, -(-2 * L2_BYTES // max(nbytes, 1)))
@@ -163,7 +166,7 @@ def time_case(case: workloads.Case, device: torch.device, trials: int = 5, graph
     for _ in range(sets):
         b = base.clone()
         b.positions = base.positions.clone()
-        b.cache = base.cache.clone()
+        b.cache = base.cache if shared_cache else base.cache.clone()
         if from_lens:
             _with_lens(case, b, device)
         buffers.append(b)
@@ -201,6 +204,7 @@ def time_case(case: workloads.Case, device: torch.device, trials: int = 5, graph
         "clocks": clocks.summary(),
         "buffer_sets": sets,
         "l2_cold": bool(sets * nbytes > 2 * L2_BYTES),
+        "cos_sin_cache": "shared by all sets" if shared_cache else "one copy per set",
         "pdl": os.environ.get("WELM_ROPE_PDL", "1") != "0",
         "entry": "rope_mirror_from_lens" if from_lens and case.is_mirror and case.is_segmented
         else "welmv4_inplace_rope_npu",
@@ -341,7 +345,7 @@ def write_csv(records: list[dict], path: str) -> None:
 
 def run(cases: Iterable[workloads.Case], device: torch.device, time_it: bool, iters: int,
         out: Optional[str], from_lens: bool = False, copy_ceiling: bool = False,
-        host_transport: Optional[str] = None) -> list[dict]:
+        host_transport: Optional[str] = None, shared_cache: bool = False) -> list[dict]:
     records = []
     sink = open(out, "a") if out else None
     try:
@@ -349,7 +353,8 @@ def run(cases: Iterable[workloads.Case], device: torch.device, time_it: bool, it
             if host_transport is not None:
                 rec = time_host_case(case, device, host_transport)
             elif time_it:
-                rec = time_case(case, device, from_lens=from_lens, copy_ceiling=copy_ceiling)
+                rec = time_case(case, device, from_lens=from_lens, copy_ceiling=copy_ceiling,
+                                shared_cache=shared_cache)
             else:
                 rec = launch_case(case, device, iters, from_lens)
             records.append(rec)
@@ -373,6 +378,8 @@ def main(argv: Optional[list[str]] = None) -> int:
     parser.add_argument("--device", default="cuda:0")
     parser.add_argument("--json", default=None, help="append JSON lines here")
     parser.add_argument("--csv", default=None, help="write all records as one CSV table here")
+    parser.add_argument("--shared-cache", action="store_true",
+                        help="with --time: one cos/sin cache for all buffer sets (hot in L2, as in serving)")
     parser.add_argument("--mirror-from-lens", action="store_true",
                         help="run segmented KV-mirror cases through rope_mirror_from_lens")
     parser.add_argument("--copy-ceiling", action="store_true",
@@ -397,7 +404,7 @@ def main(argv: Optional[list[str]] = None) -> int:
                 fh.write(json.dumps(rec) + "\n")
         return 0
     records = run(select_cases(args.cases), device, args.time, args.iters, args.json, args.mirror_from_lens,
-                  args.copy_ceiling, args.host)
+                  args.copy_ceiling, args.host, args.shared_cache)
     if args.csv:
         write_csv(records, args.csv)
     return 0
