@@ -99,15 +99,16 @@ int launch_plan(Kernel kernel, const Plan& plan, const RopeArgs& a, cudaStream_t
     const size_t smem = staged_table ? (size_t(a.num_tiles + 1) * sizeof(int32_t) + 15) & ~size_t(15) : 0;
     return launch(kernel, unsigned((total + kBlock - 1) / kBlock), kBlock, smem, stream, a);
   }
-  // A decode-sized launch (more than two warps of items, but less than one
-  // full CTA per SM) runs in warp-sized CTAs instead, so its tokens spread
-  // over several SMs rather than queueing on one SM's bandwidth: one 128-thread
-  // CTA holds 32 tokens.  Measured on one B200 (graph replay): M=32 decode
-  // 1.73 -> 1.44 us, M=128 1.70 -> 1.47 us; at 16 tokens or fewer one CTA is
-  // as fast or faster, so those keep it.
+  // A launch with more than two warps of items but fewer than two full
+  // 128-thread CTAs per SM runs in warp-sized CTAs instead.  Its tokens then
+  // spread evenly over the SMs rather than queueing on a few SMs' bandwidth
+  // (one 128-thread CTA holds 32 tokens).  Measured on one B200 (graph
+  // replay, us): decode M=32 1.73 -> 1.44 and M=128 1.70 -> 1.47, prefill
+  // M=1024 2.23 -> 1.96 and M=6145 3.62 -> 3.47.  At 16 tokens or fewer one
+  // CTA is as fast or faster, and from M=16384 the 128-thread grid is.
   constexpr int kSmallBlock = 32;
   const int sms = current_sm_count();
-  if (sms > 0 && total > 2 * kSmallBlock && total <= int64_t(sms) * kBlock) {
+  if (sms > 0 && total > 2 * kSmallBlock && total <= 2 * int64_t(sms) * kBlock) {
     return launch(kernel, unsigned((total + kSmallBlock - 1) / kSmallBlock), kSmallBlock, 0, stream, a);
   }
   return launch(kernel, grid_for(total), kBlock, 0, stream, a);
