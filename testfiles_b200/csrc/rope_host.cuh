@@ -42,6 +42,27 @@ unsigned grid_for(int64_t items) {
   return unsigned(need < cap ? need : cap);
 }
 
+// Grid and block for `total` work items of a grid-stride kernel.  A launch
+// with more than two warps of items but fewer than two full 128-thread CTAs
+// per SM runs in warp-sized CTAs instead.  Its tokens then spread evenly over
+// the SMs rather than queueing on a few SMs' bandwidth (one 128-thread CTA
+// holds 32 tokens).  Measured on one B200 (graph replay, us): decode M=32
+// 1.73 -> 1.44 and M=128 1.70 -> 1.47, prefill M=1024 2.23 -> 1.96 and
+// M=6145 3.62 -> 3.47, fused KV write N=BS=128 1.86 -> 1.51.  At 16 tokens or
+// fewer one CTA is as fast or faster, and from M=16384 the 128-thread grid is.
+struct LaunchShape {
+  unsigned grid;
+  unsigned block;
+};
+
+LaunchShape shape_for(int64_t total) {
+  constexpr int kSmallBlock = 32;
+  const int sms = current_sm_count();
+  if (sms > 0 && total > 2 * kSmallBlock && total <= 2 * int64_t(sms) * kBlock)
+    return {unsigned((total + kSmallBlock - 1) / kSmallBlock), unsigned(kSmallBlock)};
+  return {grid_for(total), unsigned(kBlock)};
+}
+
 // Launches carry the programmatic-stream-serialization attribute (PDL) unless
 // the environment sets WELM_ROPE_PDL=0: the grid may be scheduled while the
 // previous kernel in the stream drains, and waits in pdl_enter() before it
@@ -99,19 +120,8 @@ int launch_plan(Kernel kernel, const Plan& plan, const RopeArgs& a, cudaStream_t
     const size_t smem = staged_table ? (size_t(a.num_tiles + 1) * sizeof(int32_t) + 15) & ~size_t(15) : 0;
     return launch(kernel, unsigned((total + kBlock - 1) / kBlock), kBlock, smem, stream, a);
   }
-  // A launch with more than two warps of items but fewer than two full
-  // 128-thread CTAs per SM runs in warp-sized CTAs instead.  Its tokens then
-  // spread evenly over the SMs rather than queueing on a few SMs' bandwidth
-  // (one 128-thread CTA holds 32 tokens).  Measured on one B200 (graph
-  // replay, us): decode M=32 1.73 -> 1.44 and M=128 1.70 -> 1.47, prefill
-  // M=1024 2.23 -> 1.96 and M=6145 3.62 -> 3.47.  At 16 tokens or fewer one
-  // CTA is as fast or faster, and from M=16384 the 128-thread grid is.
-  constexpr int kSmallBlock = 32;
-  const int sms = current_sm_count();
-  if (sms > 0 && total > 2 * kSmallBlock && total <= 2 * int64_t(sms) * kBlock) {
-    return launch(kernel, unsigned((total + kSmallBlock - 1) / kSmallBlock), kSmallBlock, 0, stream, a);
-  }
-  return launch(kernel, grid_for(total), kBlock, 0, stream, a);
+  const LaunchShape shape = shape_for(total);
+  return launch(kernel, shape.grid, shape.block, 0, stream, a);
 }
 
 }  // namespace

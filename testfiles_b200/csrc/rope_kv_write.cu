@@ -192,7 +192,8 @@ int welm_rope_mirror_kv_write(const void* q, void* q_out, const void* k, const v
   a.q_items = int32_t(rows * kQHeads * kParts);
   a.k_items = int32_t(n_tokens * kParts);
   const int64_t total = int64_t(a.q_items) + a.k_items;
-  return launch(rope_mirror_kv_write_kernel, grid_for(total), kBlock, 0, static_cast<cudaStream_t>(stream), a);
+  const LaunchShape shape = shape_for(total);
+  return launch(rope_mirror_kv_write_kernel, shape.grid, shape.block, 0, static_cast<cudaStream_t>(stream), a);
 }
 
 }  // extern "C"
