@@ -53,6 +53,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "welm_rope_abi_version": (ctypes.c_int, []),
 }
 
+ABI_MAJOR = 1  # include/welm_rope.h: WELM_ROPE_ABI_VERSION >> 16
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
 
@@ -78,6 +79,13 @@ def load() -> ctypes.CDLL:
                     "(the sm_100a library is required; there is no fallback)"
                 )
             lib = ctypes.CDLL(str(LIBRARY))
+            lib.welm_rope_abi_version.restype = ctypes.c_int
+            major = lib.welm_rope_abi_version() >> 16
+            if major != ABI_MAJOR:
+                raise RuntimeError(
+                    f"{LIBRARY.name} has ABI major version {major}, these bindings expect {ABI_MAJOR}: "
+                    "rebuild it with `python -m testfiles_b200.build`"
+                )
             for name, (restype, argtypes) in SIGNATURES.items():
                 fn = getattr(lib, name)
                 fn.restype = restype

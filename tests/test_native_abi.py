@@ -279,3 +279,9 @@ def test_clock_sampler_without_a_device_reports_no_samples():
         pass
     summary = s.summary()
     assert summary["samples"] == 0 or summary["sm_mhz"] is not None
+
+
+def test_bindings_match_the_header_abi_major():
+    header = (REPO / "include" / "welm_rope.h").read_text()
+    major = int(re.search(r"#define WELM_ROPE_ABI_VERSION \(\((\d+) << 16\)", header).group(1))
+    assert _native.ABI_MAJOR == major
