@@ -133,3 +133,28 @@ def test_c_oracle_matches_torch_oracle_on_edge_values():
 def test_c_oracle_tile_builder_edge_lengths():
     for lens in ([], [0], [0, 0, 5], [64], [65, 0, 128, 1], [1] * 70, [4096, 3]):
         assert c_oracle.build_tiles(lens) == rope_oracle.build_tile_starts(lens), lens
+
+
+def test_c_and_torch_oracles_agree_on_random_inputs():
+    """Property check beyond the fixtures: random row and head counts,
+    positions over the whole cache (both ends included), values spanning
+    several binades.  NaN cannot arise from finite inputs here."""
+    from hypothesis import given, settings
+    from hypothesis import strategies as st
+
+    cache = rope_oracle.make_cos_sin_cache(512, 10000.0)
+
+    @settings(max_examples=60, deadline=None)
+    @given(rows=st.integers(1, 40), heads=st.sampled_from([1, 6]), seed=st.integers(0, 2**31 - 1),
+           scale=st.sampled_from([1e-3, 1.0, 300.0]))
+    def check(rows, heads, seed, scale):
+        g = torch.Generator().manual_seed(seed)
+        x = (torch.randn(rows, heads, 256, generator=g) * scale).to(torch.bfloat16)
+        pos = torch.randint(0, 512, (rows,), generator=g)
+        pos[0] = 0
+        pos[-1] = 511
+        want = rope_oracle.apply_reference(x, pos, cache)
+        got = c_oracle.apply(x, pos, cache)
+        assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+
+    check()
