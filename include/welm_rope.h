@@ -81,8 +81,10 @@ typedef enum welm_rope_status {
  * (bench_welmv4_inplace_rope_npu.py:326-405, 443-526) called with last_index = None.
  *
  *   has_segments == 0: tile i covers tokens [64 i, min(64 i + 64, N)) for
- *       i < num_work_tiles (the reference passes ceil(N/64)); the
- *       segment_tile_starts pointer is not dereferenced and may be NULL.
+ *       i < num_work_tiles (the reference passes ceil(N/64); with 0 work
+ *       tiles nothing is rotated and the call returns WELM_ROPE_OK without
+ *       touching any pointer); the segment_tile_starts pointer is not
+ *       dereferenced and may be NULL.
  *   has_segments == 1: tile i covers [starts[i], starts[i] + min(64,
  *       starts[i+1] - starts[i])) for i < num_work_tiles; N bounds the tokens.
  * Positions are gathered per token, so no contiguity inside a tile is needed.
