@@ -104,6 +104,16 @@ def _stream(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+def _call(device: torch.device, fn, *args) -> int:
+    """Run a library entry with ``device`` current: the library launches into
+    the current device's context, and the tensors' device need not be the
+    caller's current one."""
+    if device.index is None or device.index == torch.cuda.current_device():
+        return fn(*args)
+    with torch.cuda.device(device):
+        return fn(*args)
+
+
 def _status_ptr(status: Optional[torch.Tensor], device: torch.device) -> Optional[int]:
     if status is None:
         return None
@@ -153,7 +163,7 @@ def rope_prefill(
     if int(N) > positions.numel() or int(N) > k.shape[0] or int(N) > q.shape[0]:
         raise ValueError("N exceeds the rows of positions, key or query")
     lib = _native.load()
-    rc = lib.welm_rope_ordinary(
+    rc = _call(device, lib.welm_rope_ordinary,
         _ptr(q), _ptr(k), _ptr(positions), _ptr(cos_sin_cache), starts,
         int(num_work_tiles), int(N), int(q_token_stride), int(k_token_stride),
         int(has_segments), int(cos_sin_cache.shape[0]), _status_ptr(status, device), _stream(device),
@@ -193,7 +203,7 @@ def rope_mirror_prefill(
     if int(N) > positions.numel() or int(N) > k.shape[0]:
         raise ValueError("N exceeds the rows of positions or key")
     lib = _native.load()
-    rc = lib.welm_rope_mirror(
+    rc = _call(device, lib.welm_rope_mirror,
         _ptr(q), _ptr(k), _ptr(positions), _ptr(cos_sin_cache), _ptr(last_index), starts,
         int(num_work_tiles), int(N), int(BS), int(q_token_stride), int(k_token_stride),
         int(has_segments), int(cos_sin_cache.shape[0]), _status_ptr(status, device), _stream(device),
@@ -287,7 +297,7 @@ def rope_mirror_kv_write(
         raise ValueError("q, k, v and slot_mapping need one row per token")
     if q_out.shape[0] != batch:
         raise ValueError("q_out needs one row per request (last_index entry)")
-    rc = _native.load().welm_rope_mirror_kv_write(
+    rc = _call(device, _native.load().welm_rope_mirror_kv_write,
         _ptr(q), _ptr(q_out), _ptr(k), _ptr(v), _ptr(positions), _ptr(cos_sin_cache), _ptr(last_index),
         _ptr(slot_mapping), _ptr(key_cache), _ptr(value_cache), n, batch, int(q.stride(0)), int(q_out.stride(0)),
         int(k.stride(0)), int(v.stride(0)) if v is not None else 0, HEAD_DIM, key_cache.numel() // HEAD_DIM,
@@ -319,7 +329,7 @@ def rope_mirror_from_lens(
     n = int(positions.shape[0])
     if k.shape[0] != n:
         raise ValueError("key rows must equal the positions length")
-    rc = _native.load().welm_rope_mirror_from_lens(
+    rc = _call(device, _native.load().welm_rope_mirror_from_lens,
         _ptr(q), _ptr(k), _ptr(positions), _ptr(cos_sin_cache), _ptr(seq_lens), n, batch, int(q.stride(0)),
         int(k.stride(0)), int(cos_sin_cache.shape[0]), _status_ptr(status, device), _stream(device))
     _native.check("welm_rope_mirror_from_lens", rc)
@@ -397,7 +407,7 @@ def build_segment_tile_starts_device(
     starts = torch.empty(int(capacity), dtype=torch.int32, device=device)
     num_tiles = torch.empty(1, dtype=torch.int32, device=device)
     last = torch.empty(batch, dtype=torch.int64, device=device)
-    rc = _native.load().welm_rope_build_tiles(
+    rc = _call(device, _native.load().welm_rope_build_tiles,
         _ptr(lens), batch, starts.data_ptr(), int(capacity), num_tiles.data_ptr(), _ptr(last),
         _status_ptr(status, device), _stream(device),
     )

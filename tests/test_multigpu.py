@@ -95,3 +95,47 @@ def test_two_gpu_request_sharding_matches_oracle():
         p.join(timeout=120)
         assert p.exitcode == 0
     assert results == {"mirror": (True, True), "prefill": (True, True)}
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ops_on_a_device_that_is_not_current():
+    """Tensors on cuda:1 while cuda:0 is current: every op runs on the tensors'
+    device, equals the oracle, and leaves the caller's current device alone."""
+    import testfiles_b200 as welm
+    from oracle import rope_oracle
+    from testfiles_b200 import workloads
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 1)
+
+    case = workloads.find_case("b_prefill_m577")
+    inp = workloads.make_inputs(case, "cpu")
+    d = inp.to(dev)
+    welm.welmv4_inplace_rope_npu(d.query, d.key, d.positions, d.cache)
+    torch.cuda.synchronize(dev)
+    q_ref, k_ref = rope_oracle.reference_outputs(inp.query, inp.key, inp.positions, None, inp.cache)
+    assert torch.equal(d.query.cpu().view(torch.int16), q_ref.view(torch.int16))
+    assert torch.equal(d.key.cpu().view(torch.int16), k_ref.view(torch.int16))
+
+    case = workloads.find_case("b_mirror_segmented_n8192_bs8_uneven")
+    inp = workloads.make_inputs(case, "cpu")
+    q_ref, k_ref = rope_oracle.reference_outputs(inp.query, inp.key, inp.positions, inp.last_index, inp.cache)
+    d = inp.to(dev)
+    welm.welmv4_inplace_rope_npu(d.query, d.key, d.positions, d.cache, d.last_index, d.segment_tile_starts)
+    torch.cuda.synchronize(dev)
+    assert torch.equal(d.query.cpu().view(torch.int16), q_ref.view(torch.int16))
+    assert torch.equal(d.key.cpu().view(torch.int16), k_ref.view(torch.int16))
+
+    lens = torch.tensor(case.segment_lens, dtype=torch.int64, device=dev)
+    d = inp.to(dev)
+    welm.rope_mirror_from_lens(d.query, d.key, d.positions, d.cache, lens)
+    torch.cuda.synchronize(dev)
+    assert torch.equal(d.query.cpu().view(torch.int16), q_ref.view(torch.int16))
+    assert torch.equal(d.key.cpu().view(torch.int16), k_ref.view(torch.int16))
+
+    starts, num_tiles, last = welm.build_segment_tile_starts_device(lens, 8192 // 64 + len(case.segment_lens) + 1)
+    host_starts, host_tiles, host_last = welm.build_segment_tile_starts(case.segment_lens)
+    assert starts.device == dev and int(num_tiles.item()) == host_tiles
+    assert torch.equal(starts[: host_tiles + 1].cpu(), host_starts)
+    assert torch.equal(last.cpu(), host_last)
+    assert torch.cuda.current_device() == 0
