@@ -73,7 +73,7 @@ class HostRopePipeline:
         if n == 0:
             return
         current = torch.cuda.current_stream(self.device)
-        with self.lock:
+        with torch.cuda.device(self.device), self.lock:  # the pipeline's device, whatever is current
             self.h2d.wait_stream(current)
             for c, t0 in enumerate(range(0, n, self.chunk)):
                 t1 = min(n, t0 + self.chunk)

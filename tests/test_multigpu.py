@@ -138,4 +138,16 @@ def test_ops_on_a_device_that_is_not_current():
     assert starts.device == dev and int(num_tiles.item()) == host_tiles
     assert torch.equal(starts[: host_tiles + 1].cpu(), host_starts)
     assert torch.equal(last.cpu(), host_last)
+
+    from testfiles_b200 import host
+
+    case = workloads.find_case("b_prefill_m577")
+    inp = workloads.make_inputs(case, "cpu")
+    q_ref, k_ref = rope_oracle.reference_outputs(inp.query, inp.key, inp.positions, None, inp.cache)
+    for transport in ("mapped", "staged"):
+        q, k, p = inp.query.clone().pin_memory(), inp.key.clone().pin_memory(), inp.positions.pin_memory()
+        host.welmv4_inplace_rope_host(q, k, p, inp.cache.to(dev), chunk_tokens=256, transport=transport)
+        torch.cuda.synchronize(dev)
+        assert torch.equal(q.view(torch.int16), q_ref.view(torch.int16)), transport
+        assert torch.equal(k.view(torch.int16), k_ref.view(torch.int16)), transport
     assert torch.cuda.current_device() == 0
