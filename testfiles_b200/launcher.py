@@ -28,7 +28,9 @@ pipeline-fill costs weigh as much as bandwidth.
 cases): Q, K and positions in pinned host memory, every PCIe transfer inside
 the timed region, µs per call and GB/s each way over the bus.
 ``--kv-write N,BS`` times the fused KV-mirror cache write (with ``--time``;
-with ``--iters`` it only launches it, for ncu).
+with ``--iters`` it only launches it, for ncu).  ``--fused-qkv M`` times
+prefill on strided Q/K views of a fused QKV projection output beside a
+contiguous Q copy followed by the op.
 """
 
 from __future__ import annotations
@@ -316,6 +318,69 @@ def time_kv_write(n_tokens: int, batch: int, device: torch.device, trials: int =
     }
 
 
+def time_fused_qkv(n_tokens: int, device: torch.device, trials: int = 7, graph_launches: int = 32,
+                   replays: int = 20, sets: Optional[int] = None) -> dict:
+    """µs per ordinary prefill on a fused QKV projection output [N, 8 x 256]
+    (6 Q heads, the K head, the V head per token), two ways, each
+    graph-replayed over the same rotating buffer sets:
+
+    * ``strided``: the op on strided Q / K views of the QKV rows (token stride
+      2048 elements), with no copy;
+    * ``copy_then_rope``: the producer-side pattern this avoids, a contiguous
+      copy of Q out of the QKV rows and then the op on that copy (K stays
+      strided).
+
+    Positions are 0..N-1 and each set has its own cos/sin cache copy.  The
+    record gives both times and what the strided call saves."""
+    cache = workloads.make_cos_sin_cache(max(n_tokens, 1), 10000.0, device=device)
+    nbytes = 2056 * n_tokens
+    if sets is None:
+        sets = int(min(16, max(2, -(-2 * L2_BYTES // max(nbytes, 1)))))
+    g = torch.Generator(device=device).manual_seed(0)
+    bufs = []
+    for _ in range(sets):
+        qkv = torch.randn((n_tokens, 8 * 256), generator=g, device=device).to(torch.bfloat16)
+        bufs.append((qkv, torch.empty((n_tokens, 6, 256), dtype=torch.bfloat16, device=device),
+                     torch.arange(n_tokens, dtype=torch.int64, device=device), cache.clone()))
+
+    def views(qkv: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        return qkv[:, :1536].view(n_tokens, 6, 256), qkv[:, 1536:1792].view(n_tokens, 1, 256)
+
+    def strided(i: int) -> None:
+        qkv, _, pos, cs = bufs[i % sets]
+        q, k = views(qkv)
+        ops.welmv4_inplace_rope_npu(q, k, pos, cs)
+
+    def copy_then_rope(i: int) -> None:
+        qkv, q_buf, pos, cs = bufs[i % sets]
+        q, k = views(qkv)
+        q_buf.copy_(q)
+        ops.welmv4_inplace_rope_npu(q_buf, k, pos, cs)
+
+    out = {}
+    for name, call in (("strided", strided), ("copy_then_rope", copy_then_rope)):
+        for i in range(3):
+            call(i)
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(graph_launches):
+                call(i)
+        out[name] = _replay_us(graph, device, trials, replays, graph_launches)
+        del graph
+    peak, kind = measured_hbm_peak()
+    us = out["strided"]
+    return {
+        "record_type": "timing", "case": f"fused_qkv_prefill_m{n_tokens}", "phase": "prefill",
+        "path": "fused_qkv_strided", "n_tokens": n_tokens, "q_token_stride": 2048, "k_token_stride": 2048,
+        "us_per_launch": round(us, 3), "bytes_per_launch": nbytes, "gb_s": round(nbytes / (us * 1e3), 1),
+        "hbm_frac": round(nbytes / (us * 1e3) / peak, 4), "hbm_peak_gbs": peak, "hbm_peak_source": kind,
+        "copy_then_rope_us": round(out["copy_then_rope"], 3),
+        "saved_us": round(out["copy_then_rope"] - us, 3), "buffer_sets": sets,
+        "l2_cold": sets * nbytes > 2 * L2_BYTES, "device_name": torch.cuda.get_device_name(device),
+    }
+
+
 def launch_case(case: workloads.Case, device: torch.device, iters: int, from_lens: bool = False) -> dict:
     inp = workloads.make_inputs(case, device)
     if from_lens:
@@ -389,15 +454,23 @@ def main(argv: Optional[list[str]] = None) -> int:
     parser.add_argument("--kv-write", default=None, metavar="N,BS",
                         help="time the fused KV-mirror cache write for N tokens in BS requests (with --iters: "
                              "only launch it)")
+    parser.add_argument("--fused-qkv", type=int, default=None, metavar="M",
+                        help="time prefill on strided Q/K views of an [M, 8 x 256] QKV output against a "
+                             "contiguous Q copy followed by the op")
     args = parser.parse_args(argv)
     if not torch.cuda.is_available():
         print("the launcher needs a CUDA device", file=sys.stderr)
         return 2
     device = torch.device(args.device)
     torch.cuda.set_device(device)
-    if args.kv_write:
-        n, bs = (int(x) for x in args.kv_write.split(","))
-        rec = time_kv_write(n, bs, device, iters=0 if args.time else args.iters)
+    if args.kv_write or args.fused_qkv:
+        if args.fused_qkv:
+            if args.fused_qkv <= 0:
+                parser.error("--fused-qkv needs a positive token count")
+            rec = time_fused_qkv(args.fused_qkv, device)
+        else:
+            n, bs = (int(x) for x in args.kv_write.split(","))
+            rec = time_kv_write(n, bs, device, iters=0 if args.time else args.iters)
         print(json.dumps(rec), flush=True)
         if args.json:
             with open(args.json, "a") as fh:

@@ -50,3 +50,11 @@ def test_time_kv_write_record():
     assert rec["us_per_launch"] > 0 and rec["bytes_per_launch"] == launcher.kv_write_bytes(1000, 7)
     assert rec["same_size_copy_us"] > 0
     assert launcher.time_kv_write(500, 3, DEV, iters=2)["record_type"] == "launch"
+
+
+def test_time_fused_qkv_record():
+    rec = launcher.time_fused_qkv(1000, DEV, trials=2, graph_launches=4, replays=3, sets=2)
+    assert rec["path"] == "fused_qkv_strided" and rec["bytes_per_launch"] == 2056 * 1000
+    assert rec["us_per_launch"] > 0 and rec["copy_then_rope_us"] > 0
+    assert rec["saved_us"] == pytest.approx(rec["copy_then_rope_us"] - rec["us_per_launch"], abs=2e-3)
+    json.dumps(rec)
