@@ -26,7 +26,7 @@ cos/sin cache [16384, 64] (rotary base 1e4), seeded N(0,1) synthetic data.
 * ``cpu_baseline`` (rank 0, N=1 only): the reference's CPU algorithm (the
   oracle port of its torch path) on this host's cores, same workload.
 * ``other_configs`` (rank 0, N=1 only): one configuration of each other
-  judged family (prefill M=8192, decode M=1 and M=128, contiguous and
+  benchmark family (prefill M=8192, decode M=1 and M=128, contiguous and
   segmented KV mirror at N=16384) and the KV mirror fused with the paged
   KV-cache write (N=16384, BS=128), timed after the headline, with a
   same-size device copy beside each (``--no-config-sweep`` skips it).
@@ -233,7 +233,7 @@ def timed_steps(step, count: int, dist, device, stream) -> float:
     return max_over_ranks(dist, start.elapsed_time(end), device)
 
 
-# One configuration of each other judged family, timed after the headline
+# One configuration of each other benchmark family, timed after the headline
 # (rank 0, N=1) with the launcher's method: graph replay over L2-cold buffer
 # sets, plus a same-size device copy as the practical ceiling.
 OTHER_CONFIGS = ("b_prefill_m8192", "b_decode_m1", "b_decode_m128", "b_mirror_contiguous_n16384",
@@ -494,7 +494,7 @@ def main() -> int:
     parser.add_argument("--warmup", type=int, default=50)
     parser.add_argument("--e2e-steps", type=int, default=100)
     parser.add_argument("--no-config-sweep", action="store_true",
-                        help="skip the one-per-family timing of the other judged configurations")
+                        help="skip the one-per-family timing of the other benchmark configurations")
     parser.add_argument("--impl", choices=("b200", "reference"), default="b200")
     args = parser.parse_args()
     if args.steps <= 0:

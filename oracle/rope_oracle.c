@@ -1,7 +1,8 @@
 /*
  * rope_oracle.c — plain-C restatement of the reference's CPU algorithm for the
- * in-place partial RoPE.  TEST INFRASTRUCTURE ONLY: the checker, never the
- * product; tests/ and the C-ABI smoke program link it, nothing else does.
+ * in-place partial RoPE.  TEST INFRASTRUCTURE ONLY: it checks the product
+ * and is never part of it; tests/ and the C-ABI smoke program link it,
+ * nothing else does.
  *
  * welm_oracle_apply restates apply_reference (bench_welmv4_inplace_rope_npu.py:
  * 1489-1505): every head of every row is copied, then lanes 192..223 (x1) and

@@ -1,6 +1,6 @@
 """CPU oracle for WeLMv4 in-place partial RoPE — TEST INFRASTRUCTURE ONLY.
 
-This module is the checker, never the product: only ``tests/``,
+This module checks the product and is never part of it: only ``tests/``,
 ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline / reference leg
 may import it.  The product path (``testfiles_b200``) never calls it and has
 no CPU fallback.

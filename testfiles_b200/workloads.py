@@ -8,7 +8,7 @@ Two input flavours exist for every case:
   113, segmented positions ``113 + 97*request + local``, decode / legacy
   mirror positions ``(17 i + 11) % 32768``.  Used to pin parity against the
   reference's own outputs.
-* ``"baseline"`` follows the judged configurations of this port: cache base
+* ``"baseline"`` is the benchmark's own configuration set: cache base
   1e4 with 16384 rows, prefill positions ``0..M-1``, decode positions uniform
   in [0, 16383], segmented positions restarting at 0 in every request,
   seeded-uneven request lengths drawn as a uniform partition (lengths >= 1).
@@ -41,9 +41,9 @@ REFERENCE_SEED = 20260814
 REFERENCE_MAX_POSITION = 32768
 REFERENCE_ROPE_BASE = 100000.0
 REFERENCE_POSITION_START = 113
-BASELINE_SEED = 20261201
-BASELINE_MAX_POSITION = 16384
-BASELINE_ROPE_BASE = 10000.0
+BENCH_SEED = 20261201
+BENCH_MAX_POSITION = 16384
+BENCH_ROPE_BASE = 10000.0
 
 PHASES = (
     "decode",
@@ -208,7 +208,7 @@ def reference_cases() -> tuple[Case, ...]:
 
 
 def baseline_cases(include_sweeps: bool = True) -> tuple[Case, ...]:
-    """The judged configurations: M=8192 prefill, decode M=1..128, the
+    """The benchmark configurations: M=8192 prefill, decode M=1..128, the
     prefill sweep with tails, BS=1 contiguous mirror for N in {8192, 9616,
     16361, 16384}, and segmented mirror for N in {8192, 9616, 16384} x BS in
     {2..128}, equal (64-aligned) or seeded-uneven lengths."""
@@ -223,7 +223,7 @@ def baseline_cases(include_sweeps: bool = True) -> tuple[Case, ...]:
             if n % bs == 0 and (n // bs) % TILE_TOKENS == 0:
                 out.append(Case(f"b_mirror_segmented_n{n}_bs{bs}_aligned", "prefill_mirror_segmented", n, bs,
                                 (n // bs,) * bs, flavour="baseline"))
-            lens = seeded_uneven_lens(n, bs, BASELINE_SEED + 31 * n + bs)
+            lens = seeded_uneven_lens(n, bs, BENCH_SEED + 31 * n + bs)
             out.append(Case(f"b_mirror_segmented_n{n}_bs{bs}_uneven", "prefill_mirror_segmented", n, bs, lens,
                             flavour="baseline"))
     return tuple(out)
@@ -244,7 +244,7 @@ _CACHE_MEMO: dict[tuple[int, float], torch.Tensor] = {}
 
 def cache_for(flavour: str) -> torch.Tensor:
     key = ((REFERENCE_MAX_POSITION, REFERENCE_ROPE_BASE) if flavour == "reference"
-           else (BASELINE_MAX_POSITION, BASELINE_ROPE_BASE))
+           else (BENCH_MAX_POSITION, BENCH_ROPE_BASE))
     if key not in _CACHE_MEMO:
         _CACHE_MEMO[key] = make_cos_sin_cache(*key)
     return _CACHE_MEMO[key]
@@ -265,10 +265,10 @@ def _positions(case: Case) -> torch.Tensor:
         chunks = [torch.arange(length, dtype=torch.int64) for length in case.segment_lens]
         return torch.cat(chunks) if chunks else torch.empty(0, dtype=torch.int64)
     if case.phase == "decode":
-        rng = np.random.default_rng(BASELINE_SEED + 7 * n)
-        return torch.from_numpy(rng.integers(0, BASELINE_MAX_POSITION, size=n, dtype=np.int64))
+        rng = np.random.default_rng(BENCH_SEED + 7 * n)
+        return torch.from_numpy(rng.integers(0, BENCH_MAX_POSITION, size=n, dtype=np.int64))
     if case.phase == "prefill_mirror":
-        return (torch.arange(n, dtype=torch.int64) * 17 + 11) % BASELINE_MAX_POSITION
+        return (torch.arange(n, dtype=torch.int64) * 17 + 11) % BENCH_MAX_POSITION
     return torch.arange(n, dtype=torch.int64)
 
 
@@ -284,7 +284,7 @@ def _last_index(case: Case) -> Optional[torch.Tensor]:
 
 def case_seed(case: Case, seed: Optional[int] = None) -> int:
     if seed is None:
-        seed = REFERENCE_SEED if case.flavour == "reference" else BASELINE_SEED
+        seed = REFERENCE_SEED if case.flavour == "reference" else BENCH_SEED
     return seed + case.n_tokens * 17 + case.batch_size * 101
 
 

@@ -2,7 +2,7 @@
  * c_abi_smoke.c — a plain C99 caller of the library's C ABI (include/welm_rope.h),
  * the way a non-Python host binds it: no torch, only the CUDA runtime for
  * device memory.  Each entry's result is checked bit for bit against the C
- * oracle (oracle/rope_oracle.c), the test's checker.
+ * oracle (oracle/rope_oracle.c).
  *
  * Covers: welm_rope_ordinary (dense and segmented), welm_rope_mirror
  * (segmented), welm_rope_build_tiles (device) against welm_rope_build_tiles_host

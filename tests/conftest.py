@@ -1,7 +1,7 @@
 """Shared test configuration.
 
 ``-m gpu`` tests need a CUDA device (a B200); ``-m "not gpu"`` tests run on
-any CPU.  Tests import the oracle from ``oracle/`` as the checker only.
+any CPU.  Tests import the oracle from ``oracle/`` only to check results.
 """
 
 from __future__ import annotations

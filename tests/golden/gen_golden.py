@@ -12,7 +12,7 @@ functions called here), then, on the CPU:
 * for every case of the reference catalogue: the reference's own
   ``make_cos_sin_cache``, ``make_inputs`` (seed 20260814) and
   ``reference_outputs``;
-* for every judged ("baseline") configuration: inputs from
+* for every benchmark ("baseline") configuration: inputs from
   ``testfiles_b200.workloads`` run through the reference's own
   ``reference_outputs``.
 

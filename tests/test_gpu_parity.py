@@ -1,6 +1,6 @@
 """GPU parity: the sm_100a library against the oracle, bit for bit.
 
-Every case of the reference catalogue (193) and every judged configuration
+Every case of the reference catalogue (193) and every benchmark configuration
 runs through the drop-in entry ``welmv4_inplace_rope_npu`` and through the
 reference-shaped launch surfaces (``rope_prefill`` / ``rope_mirror_prefill``
 with the reference kernels' integer arguments).  Outputs must equal the
