@@ -264,7 +264,7 @@ def other_config_records(device) -> list[dict]:
 def run_b200_arm(args) -> int:
     import testfiles_b200 as welm
     from testfiles_b200 import host as welm_host
-    from testfiles_b200 import sharding, workloads
+    from testfiles_b200 import launcher, sharding, workloads
 
     rank, world, local_rank = dist_env()
     if world != args.gpus and world > 1:
@@ -379,6 +379,12 @@ def run_b200_arm(args) -> int:
                 dst.copy_(src)
         copy_ms = timed_steps(copy_graph.replay, 20, dist, device, stream) / (20 * GRAPH_LAUNCHES)
         del copy_graph, pairs
+        # Two tighter ceilings, each rank on its own (no collective): the same
+        # bytes through the library's streaming copy kernel launched like the
+        # op, and the op's own loads and stores over its buffers without the
+        # position / cos-sin gather and the arithmetic.
+        stream_copy_us = launcher.stream_copy_us(algorithmic_bytes(TOKENS), BUFFER_SETS, device, graph_launches=64)
+        slice_floor_us = launcher.slice_floor_us([(q, k) for q, k, _, _ in sets], device, graph_launches=64)
     torch.cuda.synchronize(device)
     del body, tail
     # the timed legs are done: release their device buffers before the
@@ -444,6 +450,15 @@ def run_b200_arm(args) -> int:
                 "frac_of_same_size_copy": round(copy_ms * 1e3 / (per_step_s * 1e6), 4),
                 "same_size_copy": "torch copy_ of 16.8 MB (33.7 MB of traffic) per step, graph-replayed over "
                                   "8 rotating buffer pairs like the op: the practical ceiling at this size",
+                "stream_copy_us": round(stream_copy_us, 3),
+                "frac_of_stream_copy": round(stream_copy_us / (per_step_s * 1e6), 4),
+                "stream_copy": "the library's streaming copy kernel (welm_rope_ceiling_copy: one 16-byte vector "
+                               "per thread, PDL) on the same bytes and buffer rotation",
+                "slice_floor_us": round(slice_floor_us, 3),
+                "frac_of_slice_floor": round(slice_floor_us / (per_step_s * 1e6), 4),
+                "slice_floor": "welm_rope_ceiling_slices on the op's own buffers: the same launch shape, loads "
+                               "and stores of the rope slices, without the position / cos-sin gather and "
+                               "the arithmetic",
                 "kernel": "rope_ordinary_kernel<vec,contiguous>",
                 "bytes_per_launch": algorithmic_bytes(TOKENS),
             },

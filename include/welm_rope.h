@@ -283,13 +283,31 @@ int welm_rope_ordinary_mapped(void* q, void* k, const int64_t* positions,
                               int64_t max_position, int32_t* device_status,
                               void* stream);
 
+/*
+ * Measurement kernels: the practical ceilings the RoPE kernels are timed
+ * against on the same bytes.  They rotate nothing and have no counterpart in
+ * the reference, whose benchmark compares against the NPU's nominal peak only.
+ *
+ * welm_rope_ceiling_copy copies `bytes` (a multiple of 16; both pointers
+ * 16-byte aligned, device memory) from src to dst, one 16-byte vector per
+ * thread, launched like the op.  welm_rope_ceiling_slices reads the rope
+ * slices (lanes 192..255) of K row t (1 head) and Q row t (6 heads) for
+ * t < n_tokens and writes them back unchanged: the ordinary kernel's accesses
+ * without positions, cos/sin and arithmetic (16-byte aligned bases, strides a
+ * multiple of 8 elements, else WELM_ROPE_ERR_BAD_STRIDE).
+ */
+int welm_rope_ceiling_copy(void* dst, const void* src, int64_t bytes, void* stream);
+int welm_rope_ceiling_slices(void* q, void* k, int64_t n_tokens, int64_t q_token_stride,
+                             int64_t k_token_stride, void* stream);
+
 /* Human-readable name of a welm_rope_status code (static storage). */
 const char* welm_rope_status_string(int status);
 
 /* ABI version of this header: (major << 16) | minor.  A minor bump only adds
  * entry points or status codes; a major bump changes an existing signature.
- * 1.1 added welm_rope_ordinary_mapped and WELM_ROPE_ERR_NOT_MAPPED. */
-#define WELM_ROPE_ABI_VERSION ((1 << 16) | 1)
+ * 1.1 added welm_rope_ordinary_mapped and WELM_ROPE_ERR_NOT_MAPPED; 1.2 the
+ * two measurement kernels welm_rope_ceiling_copy and welm_rope_ceiling_slices. */
+#define WELM_ROPE_ABI_VERSION ((1 << 16) | 2)
 int welm_rope_abi_version(void);
 
 #ifdef __cplusplus

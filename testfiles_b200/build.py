@@ -21,7 +21,7 @@ CSRC = PACKAGE_DIR / "csrc"
 # one translation unit per kernel family; the .cuh headers hold what they share
 SOURCES = tuple(CSRC / name for name in (
     "rope_ordinary.cu", "rope_mirror.cu", "rope_kv_write.cu", "rope_tiles.cu", "rope_host_memory.cu",
-    "rope_abi.cu"))
+    "rope_ceiling.cu", "rope_abi.cu"))
 HEADERS = (REPO_ROOT / "include" / "welm_rope.h", CSRC / "rope_device.cuh", CSRC / "rope_host.cuh")
 LIBRARY = PACKAGE_DIR / "libwelm_rope_b200.so"
 

@@ -22,7 +22,11 @@ during the timed replays; ``--csv`` writes the records as one table.
 ``--copy-ceiling`` adds the time of a plain device
 copy moving the same bytes (half read, half written), replayed and rotated
 exactly like the op: the practical ceiling at that size, where launch and
-pipeline-fill costs weigh as much as bandwidth.
+pipeline-fill costs weigh as much as bandwidth.  It gives two copies: the
+runtime's device copy (``same_size_copy_us``) and the library's streaming
+copy kernel, launched like the op (``stream_copy_us``).  Ordinary cases also
+get ``slice_floor_us``: the op's own loads and stores without its gather
+and arithmetic, over the same buffers.
 
 ``--host mapped|staged`` times the host-memory entry instead (ordinary
 cases): Q, K and positions in pinned host memory, every PCIe transfer inside
@@ -45,7 +49,7 @@ from typing import Iterable, Optional
 
 import torch
 
-from . import ops, workloads
+from . import _native, ops, workloads
 from .clocks import ClockSampler
 
 L2_BYTES = 126 * 1024 * 1024
@@ -152,6 +156,73 @@ def same_size_copy_us(nbytes: int, sets: int, device: torch.device, trials: int 
     return us
 
 
+def ceiling_copy(dst: torch.Tensor, src: torch.Tensor, nbytes: int) -> None:
+    """The library's streaming copy (welm_rope_ceiling_copy) of ``nbytes``
+    (a multiple of 16) from ``src`` to ``dst``, both CUDA, on the current
+    stream of their device."""
+    if src.device != dst.device or src.device.type != "cuda":
+        raise ValueError("ceiling_copy needs two tensors on one CUDA device")
+    if not (src.is_contiguous() and dst.is_contiguous()):
+        raise ValueError("ceiling_copy needs contiguous tensors")
+    if nbytes < 0 or nbytes > min(src.numel() * src.element_size(), dst.numel() * dst.element_size()):
+        raise ValueError("nbytes exceeds a buffer")
+    lib = _native.load()
+    rc = ops._call(dst.device, lib.welm_rope_ceiling_copy, dst.data_ptr(), src.data_ptr(), int(nbytes),
+                   torch.cuda.current_stream(dst.device).cuda_stream)
+    _native.check("welm_rope_ceiling_copy", rc)
+
+
+def ceiling_slices(q: torch.Tensor, k: torch.Tensor) -> None:
+    """The ordinary kernel's loads and stores alone (welm_rope_ceiling_slices):
+    the rope slices of every row of ``q`` [M, 6, 256] and ``k`` [M, 1, 256]
+    read and written back unchanged, on the current stream of their device."""
+    ops._check_heads(q, "query", ops.NUM_Q_HEADS)
+    ops._check_heads(k, "key", ops.NUM_K_HEADS)
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16:
+        raise TypeError("ceiling_slices needs bf16 q and k")
+    if q.device != k.device or q.device.type != "cuda" or q.shape[0] != k.shape[0]:
+        raise ValueError("ceiling_slices needs q and k with the same rows on one CUDA device")
+    lib = _native.load()
+    rc = ops._call(q.device, lib.welm_rope_ceiling_slices, q.data_ptr(), k.data_ptr(), int(q.shape[0]),
+                   int(q.stride(0)), int(k.stride(0)), torch.cuda.current_stream(q.device).cuda_stream)
+    _native.check("welm_rope_ceiling_slices", rc)
+
+
+def stream_copy_us(nbytes: int, sets: int, device: torch.device, trials: int = 5, graph_launches: int = 64,
+                   replays: int = 20) -> float:
+    """µs per streaming copy (welm_rope_ceiling_copy) of ``nbytes // 2`` bytes
+    rounded down to 16 (``nbytes`` of traffic), graph-replayed over ``sets``
+    rotating source/destination pairs like :func:`same_size_copy_us`."""
+    half = max(16, nbytes // 2 // 16 * 16)
+    pairs = [(torch.ones(half, dtype=torch.uint8, device=device), torch.empty(half, dtype=torch.uint8, device=device))
+             for _ in range(sets)]
+    ceiling_copy(pairs[0][1], pairs[0][0], half)
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(graph_launches):
+            src, dst = pairs[i % sets]
+            ceiling_copy(dst, src, half)
+    us = _replay_us(graph, device, trials, replays, graph_launches)
+    del graph, pairs
+    return us
+
+
+def slice_floor_us(buffers: list[tuple[torch.Tensor, torch.Tensor]], device: torch.device, trials: int = 5,
+                   graph_launches: int = 64, replays: int = 20) -> float:
+    """µs per welm_rope_ceiling_slices launch over the (q, k) pairs of
+    ``buffers`` in rotation: the access-pattern floor of an ordinary launch."""
+    ceiling_slices(*buffers[0])
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(graph_launches):
+            ceiling_slices(*buffers[i % len(buffers)])
+    us = _replay_us(graph, device, trials, replays, graph_launches)
+    del graph
+    return us
+
+
 def time_case(case: workloads.Case, device: torch.device, trials: int = 5, graph_launches: int = 64,
               replays: Optional[int] = None, from_lens: bool = False, copy_ceiling: bool = False,
               shared_cache: bool = False) -> dict:
@@ -184,13 +255,19 @@ def time_case(case: workloads.Case, device: torch.device, trials: int = 5, graph
         replays = max(5, min(200, int(5e3 / (est_us * graph_launches))))
     with ClockSampler(device.index) as clocks:
         us = _replay_us(graph, device, trials, replays, graph_launches)
-    del graph, buffers
+    del graph
+    ceiling = {}
+    if copy_ceiling and not case.is_mirror and not case.is_segmented:
+        floor_us = slice_floor_us([(b.query, b.key) for b in buffers], device, trials, graph_launches, replays)
+        ceiling = {"slice_floor_us": round(floor_us, 3), "frac_of_slice_floor": round(floor_us / us, 4)}
+    del buffers
     peak, kind = measured_hbm_peak()
     gbs = nbytes / (us * 1e3)
-    ceiling = {}
     if copy_ceiling:
         copy_us = same_size_copy_us(nbytes, sets, device, trials, graph_launches, replays)
-        ceiling = {"same_size_copy_us": round(copy_us, 3), "frac_of_same_size_copy": round(copy_us / us, 4)}
+        stream_us = stream_copy_us(nbytes, sets, device, trials, graph_launches, replays)
+        ceiling.update({"same_size_copy_us": round(copy_us, 3), "frac_of_same_size_copy": round(copy_us / us, 4),
+                        "stream_copy_us": round(stream_us, 3), "frac_of_stream_copy": round(stream_us / us, 4)})
     return {
         "record_type": "timing",
         **case_fields(case),

@@ -25,6 +25,8 @@ def test_time_case_with_copy_ceiling(name):
     assert 0 < rec["frac_of_same_size_copy"] < 10
     assert rec["gb_s"] == pytest.approx(rec["bytes_per_launch"] / (rec["us_per_launch"] * 1e3), rel=0.01)
     assert set(rec["clocks"]) >= {"sm_mhz", "sm_max_mhz", "reasons", "samples"}
+    assert rec["stream_copy_us"] > 0 and rec["frac_of_stream_copy"] > 0
+    assert ("slice_floor_us" in rec) == (not case.is_mirror)
     json.dumps(rec)
 
 
@@ -58,3 +60,28 @@ def test_time_fused_qkv_record():
     assert rec["us_per_launch"] > 0 and rec["copy_then_rope_us"] > 0
     assert rec["saved_us"] == pytest.approx(rec["copy_then_rope_us"] - rec["us_per_launch"], abs=2e-3)
     json.dumps(rec)
+
+
+def test_ceiling_kernels_copy_exactly_and_leave_slices_unchanged():
+    g = torch.Generator(device=DEV).manual_seed(5)
+    src = torch.randint(0, 256, (1 << 20,), dtype=torch.uint8, device=DEV, generator=g)
+    dst = torch.zeros_like(src)
+    launcher.ceiling_copy(dst, src, (1 << 20) - 4096)
+    torch.cuda.synchronize()
+    assert torch.equal(dst[: (1 << 20) - 4096], src[: (1 << 20) - 4096])
+    assert int(dst[(1 << 20) - 4096:].count_nonzero()) == 0  # nothing past nbytes
+    with pytest.raises(ValueError):
+        launcher.ceiling_copy(dst, src, (1 << 20) + 16)
+
+    m = 3001
+    qkv = torch.randn((m, 8 * 256), device=DEV, generator=g).to(torch.bfloat16)
+    before = qkv.clone()
+    launcher.ceiling_slices(qkv[:, :1536].view(m, 6, 256), qkv[:, 1536:1792].view(m, 1, 256))
+    q = torch.randn((m, 6, 256), device=DEV, generator=g).to(torch.bfloat16)
+    k = torch.randn((m, 1, 256), device=DEV, generator=g).to(torch.bfloat16)
+    q0, k0 = q.clone(), k.clone()
+    launcher.ceiling_slices(q, k)
+    torch.cuda.synchronize()
+    assert torch.equal(qkv.view(torch.int16), before.view(torch.int16))
+    assert torch.equal(q.view(torch.int16), q0.view(torch.int16))
+    assert torch.equal(k.view(torch.int16), k0.view(torch.int16))

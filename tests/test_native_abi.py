@@ -285,3 +285,21 @@ def test_bindings_match_the_header_abi_major():
     header = (REPO / "include" / "welm_rope.h").read_text()
     major = int(re.search(r"#define WELM_ROPE_ABI_VERSION \(\((\d+) << 16\)", header).group(1))
     assert _native.ABI_MAJOR == major
+
+
+def test_ceiling_entries_host_validation():
+    """The measurement kernels refuse bad sizes, NULL and misaligned buffers
+    on the host; only valid calls would reach a launch (none here)."""
+    lib = _native.load()
+    copy, slices = lib.welm_rope_ceiling_copy, lib.welm_rope_ceiling_slices
+    assert copy(FAKE, FAKE, -16, None) == _native.ERR_BAD_SIZE
+    assert copy(FAKE, FAKE, 24, None) == _native.ERR_BAD_SIZE  # not a multiple of 16
+    assert copy(None, None, 0, None) == _native.OK
+    assert copy(None, FAKE, 16, None) == _native.ERR_NULL_POINTER
+    assert copy(FAKE + 8, FAKE, 16, None) == _native.ERR_BAD_STRIDE
+    assert slices(FAKE, FAKE, -1, 1536, 256, None) == _native.ERR_BAD_SIZE
+    assert slices(None, None, 0, 0, 0, None) == _native.OK
+    assert slices(FAKE, None, 4, 1536, 256, None) == _native.ERR_NULL_POINTER
+    assert slices(FAKE, FAKE, 4, 1535, 256, None) == _native.ERR_BAD_STRIDE
+    assert slices(FAKE, FAKE, 4, 1540, 256, None) == _native.ERR_BAD_STRIDE  # not 8-aligned
+    assert slices(FAKE, FAKE + 2, 4, 1536, 256, None) == _native.ERR_BAD_STRIDE
