@@ -4,13 +4,16 @@
 //
 // * welm_rope_ceiling_copy: a streaming device copy, one 16-byte vector per
 //   thread, launched like the op (PDL attribute, pdl_enter before the first
-//   access).  It is the best copy found for the op's byte counts, faster at
-//   these sizes than the runtime's device-to-device copy.
-// * welm_rope_ceiling_slices: the ordinary kernel's own access pattern — the
-//   same item mapping, launch shape and 16-byte loads and stores of the rope
-//   slices of K and the six Q heads, in place — without the position and
-//   cos/sin gather and without the arithmetic.  Its time is the floor of that
-//   access pattern: what the op would take if the rotation were free.
+//   access).  At a few MB and below it is faster than the runtime's
+//   device-to-device copy (8.7 MB: 2.80 against 3.26 us); at tens of MB it is
+//   slower (33.7 MB: 8.9 against 6.7-7.1 us).
+// * welm_rope_ceiling_slices: the ordinary dense kernel's own access pattern —
+//   the same item mapping (seven heads per thread, or one head per thread for
+//   launches of at most 4096 tokens), launch shape and 16-byte loads and
+//   stores of the rope slices of K and the six Q heads, in place — without
+//   the position and cos/sin gather and without the arithmetic.  Its time is
+//   the floor of that access pattern: what the op would take if the rotation
+//   were free.
 
 #include "rope_host.cuh"
 
@@ -53,6 +56,23 @@ __global__ void __launch_bounds__(kBlock) ceiling_slices_kernel(uint16_t* q, uin
   }
 }
 
+// The same for launches that the ordinary path runs one head per thread
+// (item = ((token * 7 + head) * 4 + part), head 0 the K head).
+__global__ void __launch_bounds__(kBlock) ceiling_slices_head_kernel(uint16_t* q, uint16_t* k, int64_t q_stride,
+                                                                     int64_t k_stride, int32_t items,
+                                                                     uint32_t salt) {
+  pdl_enter();
+  const int item = blockIdx.x * blockDim.x + threadIdx.x;  // the grid covers every item once
+  if (item >= items) return;
+  const int part = item & (kParts - 1);
+  const int slice = item >> kPartShift;
+  const int64_t tok = slice / kHeadsPerToken;
+  const int head = slice - int(tok) * kHeadsPerToken;
+  Slices<true, 1> x;
+  x.load(head == 0 ? k + tok * k_stride : q + tok * q_stride + (head - 1) * kHeadDim, part);
+  store_back(x, salt);
+}
+
 }  // namespace
 
 extern "C" {
@@ -78,9 +98,15 @@ int welm_rope_ceiling_slices(void* q, void* k, int64_t n_tokens, int64_t q_token
     return WELM_ROPE_ERR_BAD_STRIDE;
   if (!aligned16(q) || !aligned16(k) || q_token_stride % 8 != 0 || k_token_stride % 8 != 0)
     return WELM_ROPE_ERR_BAD_STRIDE;  // the 16-byte vector path only
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  LaunchShape shape;
+  if (head_split_shape(n_tokens, shape))
+    return launch(ceiling_slices_head_kernel, shape.grid, shape.block, 0, st, static_cast<uint16_t*>(q),
+                  static_cast<uint16_t*>(k), q_token_stride, k_token_stride,
+                  int32_t(n_tokens * kHeadsPerToken * kParts), uint32_t(0));
   const int64_t items = n_tokens * kParts;
-  const LaunchShape shape = shape_for(items);
-  return launch(ceiling_slices_kernel, shape.grid, shape.block, 0, static_cast<cudaStream_t>(stream),
+  shape = shape_for(items);
+  return launch(ceiling_slices_kernel, shape.grid, shape.block, 0, st,
                 static_cast<uint16_t*>(q), static_cast<uint16_t*>(k), q_token_stride, k_token_stride,
                 int32_t(items), uint32_t(0));
 }

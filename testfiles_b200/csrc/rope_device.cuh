@@ -48,6 +48,7 @@ constexpr int kTile = WELM_ROPE_TILE_TOKENS;        // 64
 constexpr int kLanes = 8;                           // x1 lanes owned by one thread
 constexpr int kParts = kHalf / kLanes;              // 4 threads per row slice
 constexpr int kPartShift = 2;                       // log2(kParts)
+constexpr int kHeadsPerToken = 1 + kQHeads;         // K head + 6 Q heads
 constexpr int kBlock = 128;                         // threads per CTA
 constexpr int kMaxDevices = 64;
 

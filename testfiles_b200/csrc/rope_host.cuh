@@ -63,6 +63,24 @@ LaunchShape shape_for(int64_t total) {
   return {grid_for(total), unsigned(kBlock)};
 }
 
+// Dense launches of at most this many tokens run one head per thread (the
+// ordinary one-head kernel, and the slice ceiling that mirrors it).  Measured
+// on one B200 (graph replay, L2-cold sets, us per launch, seven heads per
+// thread -> one): M=1 1.12 -> 0.86, M=8 1.22 -> 0.94, M=32 1.35 -> 1.09,
+// M=128 1.47 -> 1.15, M=256 1.49 -> 1.18, M=577 1.61 -> 1.35, M=1024
+// 1.96 -> 1.70, M=2048 2.30 -> 2.07, M=4096 2.87 -> 2.85 (even).
+constexpr int64_t kHeadSplitMaxTokens = 4096;
+
+// Launch shape of a one-head launch over `tokens` tokens: true when it
+// applies, that is at most kHeadSplitMaxTokens tokens and a grid that gives
+// every (token, head, part) item its own thread.
+bool head_split_shape(int64_t tokens, LaunchShape& shape) {
+  if (tokens > kHeadSplitMaxTokens) return false;
+  const int64_t items = tokens * kHeadsPerToken * kParts;
+  shape = shape_for(items);
+  return int64_t(shape.grid) * shape.block >= items;
+}
+
 // Launches carry the programmatic-stream-serialization attribute (PDL) unless
 // the environment sets WELM_ROPE_PDL=0: the grid may be scheduled while the
 // previous kernel in the stream drains, and waits in pdl_enter() before it

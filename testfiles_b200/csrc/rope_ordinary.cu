@@ -83,8 +83,6 @@ __global__ void __launch_bounds__(kBlock) rope_ordinary_kernel(const RopeArgs a)
 // heads.  A decode-sized launch then spreads its loads and stores over seven
 // times as many threads and SMs; every thread gathers its part of the cos/sin
 // row itself (L1/L2 hits after the first).  Same arithmetic, same results.
-constexpr int kHeadsPerToken = 1 + kQHeads;
-
 template <bool kVec>
 __global__ void __launch_bounds__(kBlock) rope_ordinary_head_kernel(const RopeArgs a) {
   const int item = blockIdx.x * blockDim.x + threadIdx.x;  // the grid covers every item once
@@ -112,21 +110,16 @@ __global__ void __launch_bounds__(kBlock) rope_ordinary_head_kernel(const RopeAr
   x.rotate_store(g.cs);
 }
 
-// Dense launches of at most this many tokens take the one-head kernel.
-// Measured on one B200 (graph replay, L2-cold sets, us per launch, seven heads
-// per thread -> one): M=1 1.12 -> 0.86, M=8 1.22 -> 0.94, M=32 1.35 -> 1.09,
-// M=128 1.47 -> 1.15, M=256 1.49 -> 1.18, M=577 1.61 -> 1.35, M=1024
-// 1.96 -> 1.70, M=2048 2.30 -> 2.07, M=4096 2.87 -> 2.85 (even).
-constexpr int64_t kHeadSplitMaxTokens = 4096;
-
 template <bool kVec>
 int launch_ordinary(const Plan& plan, const RopeArgs& a, cudaStream_t s) {
-  if (plan.src == Source::kDense && plan.token_items / kParts <= kHeadSplitMaxTokens) {
-    RopeArgs h = a;
-    h.k_items = int32_t(plan.token_items * kHeadsPerToken);
-    const LaunchShape shape = shape_for(h.k_items);
-    if (int64_t(shape.grid) * shape.block >= h.k_items)  // one item per thread, never a grid-stride loop
+  if (plan.src == Source::kDense) {
+    const int64_t items = plan.token_items * kHeadsPerToken;
+    LaunchShape shape;
+    if (head_split_shape(plan.token_items / kParts, shape)) {
+      RopeArgs h = a;
+      h.k_items = int32_t(items);
       return launch(rope_ordinary_head_kernel<kVec>, shape.grid, shape.block, 0, s, h);
+    }
   }
   switch (plan.src) {
     case Source::kDense: return launch_plan(rope_ordinary_kernel<kVec, Source::kDense>, plan, a, s);
