@@ -2,11 +2,12 @@
 // kernels are timed against on the same bytes.  They rotate nothing, read no
 // positions and no cos/sin cache, and are not part of the op.
 //
-// * welm_rope_ceiling_copy: a streaming device copy, one 16-byte vector per
-//   thread, launched like the op (PDL attribute, pdl_enter before the first
-//   access).  At a few MB and below it is faster than the runtime's
-//   device-to-device copy (8.7 MB: 2.80 against 3.26 us); at tens of MB it is
-//   slower (33.7 MB: 8.9 against 6.7-7.1 us).
+// * welm_rope_ceiling_copy: a streaming device copy launched like the op (PDL
+//   attribute, pdl_enter before the first access): one 16-byte vector per
+//   thread up to one full-occupancy wave of threads, four per thread (all
+//   loaded before any is stored) in one wave above that.  With one vector
+//   per thread at every size, 33.7 MB took 8.9 us against 6.7-7.1 us for the
+//   runtime's device-to-device copy; at 8.7 MB it took 2.80 against 3.26.
 // * welm_rope_ceiling_slices: the ordinary dense kernel's own access pattern —
 //   the same item mapping (seven heads per thread, or one head per thread for
 //   launches of at most 4096 tokens), launch shape and 16-byte loads and
@@ -19,11 +20,22 @@
 
 namespace {
 
+// kPer vectors per thread per round, all loaded before any is stored; vector
+// j of a round sits `threads` apart, so every load and store is coalesced.
+template <int kPer>
 __global__ void __launch_bounds__(kBlock) ceiling_copy_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst,
                                                               int64_t vectors) {
   pdl_enter();
-  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i < vectors) dst[i] = __ldg(src + i);
+  const int64_t threads = int64_t(gridDim.x) * blockDim.x;
+  for (int64_t base = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; base < vectors; base += threads * kPer) {
+    uint4 v[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j)
+      if (base + j * threads < vectors) v[j] = __ldg(src + base + j * threads);
+#pragma unroll
+    for (int j = 0; j < kPer; ++j)
+      if (base + j * threads < vectors) dst[base + j * threads] = v[j];
+  }
 }
 
 // Writes the loaded slices back XORed with `salt`.  The caller passes 0, so
@@ -84,9 +96,18 @@ int welm_rope_ceiling_copy(void* dst, const void* src, int64_t bytes, void* stre
   if (vectors == 0) return WELM_ROPE_OK;
   if (!dst || !src) return WELM_ROPE_ERR_NULL_POINTER;
   if (!aligned16(dst) || !aligned16(src)) return WELM_ROPE_ERR_BAD_STRIDE;
-  const unsigned grid = unsigned((vectors + kBlock - 1) / kBlock);
-  return launch(ceiling_copy_kernel, grid, kBlock, 0, static_cast<cudaStream_t>(stream),
-                static_cast<const uint4*>(src), static_cast<uint4*>(dst), vectors);
+  // Up to one full-occupancy wave of threads (16 CTAs of 128 per SM): one
+  // vector per thread.  Above that, four per thread in at most one wave.
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int sms = current_sm_count();
+  const int64_t wave = int64_t(sms > 0 ? sms : 1) * 16 * kBlock;
+  const auto* s4 = static_cast<const uint4*>(src);
+  auto* d4 = static_cast<uint4*>(dst);
+  if (vectors <= wave)
+    return launch(ceiling_copy_kernel<1>, unsigned((vectors + kBlock - 1) / kBlock), kBlock, 0, st, s4, d4, vectors);
+  const int64_t need = (vectors + 4 * kBlock - 1) / (4 * kBlock);
+  const int64_t grid = need < wave / kBlock ? need : wave / kBlock;
+  return launch(ceiling_copy_kernel<4>, unsigned(grid), kBlock, 0, st, s4, d4, vectors);
 }
 
 int welm_rope_ceiling_slices(void* q, void* k, int64_t n_tokens, int64_t q_token_stride, int64_t k_token_stride,

@@ -64,14 +64,17 @@ def test_time_fused_qkv_record():
 
 def test_ceiling_kernels_copy_exactly_and_leave_slices_unchanged():
     g = torch.Generator(device=DEV).manual_seed(5)
-    src = torch.randint(0, 256, (1 << 20,), dtype=torch.uint8, device=DEV, generator=g)
-    dst = torch.zeros_like(src)
-    launcher.ceiling_copy(dst, src, (1 << 20) - 4096)
-    torch.cuda.synchronize()
-    assert torch.equal(dst[: (1 << 20) - 4096], src[: (1 << 20) - 4096])
-    assert int(dst[(1 << 20) - 4096:].count_nonzero()) == 0  # nothing past nbytes
+    # one vector per thread; four per thread in one wave; four per thread over
+    # two rounds with a remainder
+    for size, nbytes in ((1 << 20, (1 << 20) - 4096), (8 << 20, 8 << 20), ((20 << 20) + 4096, (20 << 20) + 48)):
+        src = torch.randint(0, 256, (size,), dtype=torch.uint8, device=DEV, generator=g)
+        dst = torch.zeros_like(src)
+        launcher.ceiling_copy(dst, src, nbytes)
+        torch.cuda.synchronize()
+        assert torch.equal(dst[:nbytes], src[:nbytes]), nbytes
+        assert int(dst[nbytes:].count_nonzero()) == 0, nbytes  # nothing past nbytes
     with pytest.raises(ValueError):
-        launcher.ceiling_copy(dst, src, (1 << 20) + 16)
+        launcher.ceiling_copy(dst, src, size + 16)
 
     m = 3001
     qkv = torch.randn((m, 8 * 256), device=DEV, generator=g).to(torch.bfloat16)
