@@ -5,7 +5,8 @@
     python -m testfiles_b200.launcher --cases b_prefill_m16384 --host mapped
 
 ``--iters N`` launches the op N times eagerly on one buffer set with a fixed
-kernel name per path (``rope_ordinary_kernel`` / ``rope_mirror_kernel``), for
+kernel name per path (``rope_ordinary_head_kernel`` for dense launches of at
+most 4096 tokens, else ``rope_ordinary_kernel``; ``rope_mirror_kernel``), for
 ``ncu -k regex:…`` captures — the B200 analogue of the reference's msprof
 launch stub (run_welmv4_inplace_rope_prod_m16384_npu.py:1-60).
 
@@ -458,6 +459,20 @@ def time_fused_qkv(n_tokens: int, device: torch.device, trials: int = 7, graph_l
     }
 
 
+# Dense ordinary launches of at most this many tokens run one head per thread
+# (kHeadSplitMaxTokens in csrc/rope_host.cuh).
+HEAD_SPLIT_MAX_TOKENS = 4096
+
+
+def kernel_name(case: workloads.Case) -> str:
+    """The kernel a case's launch runs, for ``ncu -k`` filters."""
+    if case.is_mirror:
+        return "rope_mirror_kernel"
+    if not case.is_segmented and case.n_tokens <= HEAD_SPLIT_MAX_TOKENS:
+        return "rope_ordinary_head_kernel"
+    return "rope_ordinary_kernel"
+
+
 def launch_case(case: workloads.Case, device: torch.device, iters: int, from_lens: bool = False) -> dict:
     inp = workloads.make_inputs(case, device)
     if from_lens:
@@ -466,7 +481,7 @@ def launch_case(case: workloads.Case, device: torch.device, iters: int, from_len
         _launch(inp)
     torch.cuda.synchronize(device)
     return {"record_type": "launch", **case_fields(case), "iters": iters,
-            "kernel_name": "rope_mirror_kernel" if case.is_mirror else "rope_ordinary_kernel"}
+            "kernel_name": kernel_name(case)}
 
 
 def write_csv(records: list[dict], path: str) -> None:

@@ -33,7 +33,7 @@ def test_time_case_with_copy_ceiling(name):
 def test_launch_records_and_json_sink(tmp_path):
     out = tmp_path / "records.jsonl"
     recs = launcher.run(launcher.select_cases("b_prefill_m577"), DEV, False, 2, str(out))
-    assert recs[0]["record_type"] == "launch" and recs[0]["kernel_name"] == "rope_ordinary_kernel"
+    assert recs[0]["record_type"] == "launch" and recs[0]["kernel_name"] == "rope_ordinary_head_kernel"
     assert json.loads(out.read_text().splitlines()[0])["case"] == "b_prefill_m577"
 
 

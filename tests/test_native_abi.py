@@ -303,3 +303,16 @@ def test_ceiling_entries_host_validation():
     assert slices(FAKE, FAKE, 4, 1535, 256, None) == _native.ERR_BAD_STRIDE
     assert slices(FAKE, FAKE, 4, 1540, 256, None) == _native.ERR_BAD_STRIDE  # not 8-aligned
     assert slices(FAKE, FAKE + 2, 4, 1536, 256, None) == _native.ERR_BAD_STRIDE
+
+
+def test_launcher_kernel_names_follow_the_head_split_rule():
+    from testfiles_b200 import launcher, workloads
+
+    src = (REPO / "testfiles_b200" / "csrc" / "rope_host.cuh").read_text()
+    limit = int(re.search(r"constexpr int64_t kHeadSplitMaxTokens = (\d+);", src).group(1))
+    assert launcher.HEAD_SPLIT_MAX_TOKENS == limit
+    assert launcher.kernel_name(workloads.find_case("b_decode_m1")) == "rope_ordinary_head_kernel"
+    assert launcher.kernel_name(workloads.find_case("b_prefill_m4096")) == "rope_ordinary_head_kernel"
+    assert launcher.kernel_name(workloads.find_case("b_prefill_m4097")) == "rope_ordinary_kernel"
+    assert launcher.kernel_name(workloads.find_case("segmented_m4096_b8_aligned")) == "rope_ordinary_kernel"
+    assert launcher.kernel_name(workloads.find_case("b_mirror_contiguous_n8192")) == "rope_mirror_kernel"
