@@ -289,8 +289,9 @@ int welm_rope_ordinary_mapped(void* q, void* k, const int64_t* positions,
  * the reference, whose benchmark compares against the NPU's nominal peak only.
  *
  * welm_rope_ceiling_copy copies `bytes` (a multiple of 16; both pointers
- * 16-byte aligned, device memory) from src to dst, one 16-byte vector per
- * thread, launched like the op.  welm_rope_ceiling_slices reads the rope
+ * 16-byte aligned, device memory) from src to dst in 16-byte vectors (one per
+ * thread up to a full-occupancy wave, four per thread above), launched like
+ * the op.  welm_rope_ceiling_slices reads the rope
  * slices (lanes 192..255) of K row t (1 head) and Q row t (6 heads) for
  * t < n_tokens and writes them back unchanged: the ordinary kernel's accesses
  * without positions, cos/sin and arithmetic (16-byte aligned bases, strides a
