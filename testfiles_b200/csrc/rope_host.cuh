@@ -135,7 +135,15 @@ template <typename Kernel>
 int launch_plan(Kernel kernel, const Plan& plan, const RopeArgs& a, cudaStream_t stream, bool staged_table = true) {
   const int64_t total = int64_t(a.q_items) + plan.token_items + plan.check_items;
   if (plan.src == Source::kTileTable) {
+    // One item per thread.  Up to one 128-thread CTA's worth of items per SM
+    // the launch runs in warp-sized CTAs, so it spreads over all SMs instead
+    // of leaving most with one CTA.  Measured on one B200 (graph replay, us):
+    // segmented prefill M=4096 (8 requests) 3.55 -> 3.23; at M=8192 (32
+    // requests, above this limit) warp-sized CTAs were slower, 4.43 -> 4.66.
     const size_t smem = staged_table ? (size_t(a.num_tiles + 1) * sizeof(int32_t) + 15) & ~size_t(15) : 0;
+    const int sms = current_sm_count();
+    if (sms > 0 && total <= int64_t(sms) * kBlock)
+      return launch(kernel, unsigned((total + 31) / 32), 32u, smem, stream, a);
     return launch(kernel, unsigned((total + kBlock - 1) / kBlock), kBlock, smem, stream, a);
   }
   const LaunchShape shape = shape_for(total);
