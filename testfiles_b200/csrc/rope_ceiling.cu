@@ -3,18 +3,20 @@
 // positions and no cos/sin cache, and are not part of the op.
 //
 // * welm_rope_ceiling_copy: a streaming device copy launched like the op (PDL
-//   attribute, pdl_enter before the first access): one 16-byte vector per
-//   thread up to one full-occupancy wave of threads, four per thread (all
-//   loaded before any is stored) in one wave above that.  With one vector
-//   per thread at every size, 33.7 MB took 8.9 us against 6.7-7.1 us for the
-//   runtime's device-to-device copy; at 8.7 MB it took 2.80 against 3.26.
-// * welm_rope_ceiling_slices: the ordinary dense kernel's own access pattern —
+//   attribute, pdl_enter before the first access, and the source lines of
+//   each thread's first round prefetched into L2 before the wait, as the op
+//   does): one 16-byte vector per thread up to one full-occupancy wave of
+//   threads, four per thread (all loaded before any is stored) in one wave
+//   above that.  With one vector per thread at every size, 33.7 MB took
+//   8.9 us against 6.7-7.1 us for the runtime's device-to-device copy; at
+//   8.7 MB it took 2.80 against 3.26.
+// * welm_rope_ceiling_slices: the ordinary dense kernels' own access pattern —
 //   the same item mapping (seven heads per thread, or one head per thread for
-//   launches of at most 4096 tokens), launch shape and 16-byte loads and
-//   stores of the rope slices of K and the six Q heads, in place — without
-//   the position and cos/sin gather and without the arithmetic.  Its time is
-//   the floor of that access pattern: what the op would take if the rotation
-//   were free.
+//   launches of at most 4096 tokens), launch shape, pre-wait prefetch of the
+//   slice lines, and 16-byte loads and stores of the rope slices of K and the
+//   six Q heads, in place — without the position and cos/sin gather and
+//   without the arithmetic.  Its time is the floor of that access pattern:
+//   what the op would take if the rotation were free.
 
 #include "rope_host.cuh"
 
@@ -25,8 +27,16 @@ namespace {
 template <int kPer>
 __global__ void __launch_bounds__(kBlock) ceiling_copy_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst,
                                                               int64_t vectors) {
-  pdl_enter();
   const int64_t threads = int64_t(gridDim.x) * blockDim.x;
+  {  // before the wait: one prefetch per 128-byte source line of the first round
+    const int64_t base = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int64_t v = base + j * threads;
+      if (v < vectors && (v & 7) == 0) prefetch_line(src + v);
+    }
+  }
+  pdl_enter();
   for (int64_t base = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; base < vectors; base += threads * kPer) {
     uint4 v[kPer];
 #pragma unroll
@@ -52,13 +62,17 @@ __device__ __forceinline__ void store_back(Slices<true, NH>& x, uint32_t salt) {
   }
 }
 
-__global__ void __launch_bounds__(kBlock) ceiling_slices_kernel(uint16_t* q, uint16_t* k, int64_t q_stride,
-                                                                int64_t k_stride, int32_t items, uint32_t salt) {
-  pdl_enter();
+__global__ void __launch_bounds__(kBlock, 5) ceiling_slices_kernel(uint16_t* q, uint16_t* k, int64_t q_stride,
+                                                                   int64_t k_stride, int32_t items, uint32_t salt) {
   const int stride = gridDim.x * blockDim.x;
-  for (int item = blockIdx.x * blockDim.x + threadIdx.x; item < items; item += stride) {
+  const int first = blockIdx.x * blockDim.x + threadIdx.x;
+  if (first < items) prefetch_token<true>(q, k, q_stride, k_stride, first >> kPartShift, first & (kParts - 1));
+  pdl_enter();
+  for (int item = first; item < items; item += stride) {
     const int part = item & (kParts - 1);
     const int64_t tok = item >> kPartShift;
+    const int next = item + stride;
+    if (next < items) prefetch_token<true>(q, k, q_stride, k_stride, next >> kPartShift, next & (kParts - 1));
     Slices<true, 1> kx;
     Slices<true, kQHeads> qx;
     kx.load(k + tok * k_stride, part);
@@ -73,15 +87,17 @@ __global__ void __launch_bounds__(kBlock) ceiling_slices_kernel(uint16_t* q, uin
 __global__ void __launch_bounds__(kBlock) ceiling_slices_head_kernel(uint16_t* q, uint16_t* k, int64_t q_stride,
                                                                      int64_t k_stride, int32_t items,
                                                                      uint32_t salt) {
-  pdl_enter();
   const int item = blockIdx.x * blockDim.x + threadIdx.x;  // the grid covers every item once
-  if (item >= items) return;
   const int part = item & (kParts - 1);
   const int slice = item >> kPartShift;
   const int64_t tok = slice / kHeadsPerToken;
   const int head = slice - int(tok) * kHeadsPerToken;
+  uint16_t* row = head == 0 ? k + tok * k_stride : q + tok * q_stride + (head - 1) * kHeadDim;
+  if (item < items && part == 0) prefetch_row_slices<1>(row, 0);
+  pdl_enter();
+  if (item >= items) return;
   Slices<true, 1> x;
-  x.load(head == 0 ? k + tok * k_stride : q + tok * q_stride + (head - 1) * kHeadDim, part);
+  x.load(row, part);
   store_back(x, salt);
 }
 
@@ -126,7 +142,7 @@ int welm_rope_ceiling_slices(void* q, void* k, int64_t n_tokens, int64_t q_token
                   static_cast<uint16_t*>(k), q_token_stride, k_token_stride,
                   int32_t(n_tokens * kHeadsPerToken * kParts), uint32_t(0));
   const int64_t items = n_tokens * kParts;
-  shape = shape_for(items);
+  shape = stream_shape(items);
   return launch(ceiling_slices_kernel, shape.grid, shape.block, 0, st,
                 static_cast<uint16_t*>(q), static_cast<uint16_t*>(k), q_token_stride, k_token_stride,
                 int32_t(items), uint32_t(0));

@@ -119,6 +119,31 @@ __device__ __forceinline__ void prefetch_cos_sin_row(const float* cache, int64_t
     asm volatile("prefetch.global.L2 [%0];" ::"l"(cache + pos_hint * kRopeDim + part * kHalf));
 }
 
+__device__ __forceinline__ void prefetch_line(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// Prefetches the rope-slice lines of one row of NH heads (head stride 256
+// lanes) into L2, the row's four parts sharing the work: part p takes heads
+// p, p + 4, ...  A head's 64 rope lanes are 128 bytes at byte offset 384 of
+// the head: one 128-byte line when the row is 128-byte aligned (packed and
+// fused-QKV layouts from an aligned base), else two, and then both are asked
+// for.  Every address lies inside the row's rope slices.
+template <int NH>
+__device__ __forceinline__ void prefetch_row_slices(const uint16_t* row, int part) {
+  const uint16_t* slice = row + kRopeLane0;
+  const bool straddles = (reinterpret_cast<uintptr_t>(slice) & 127u) != 0;
+#pragma unroll
+  for (int h = part; h < NH; h += kParts) {
+    prefetch_line(slice + h * kHeadDim);
+    if (straddles) prefetch_line(slice + h * kHeadDim + kRopeDim - 1);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Loads / stores.  kVec: 16-byte vectors (bases 16-byte aligned, strides a
 // multiple of 8 elements); otherwise 2-byte scalars with the same results.
@@ -229,6 +254,24 @@ struct Slices {
   }
 };
 
+// The rope-slice lines of token `tok` that part `part` prefetches: the
+// token's seven slices (K, then Q heads 0..5) are shared out so that part p
+// takes slices p and p + 4.  The scalar path's rows need not be 16-byte
+// aligned, so it prefetches nothing.
+template <bool kVec>
+__device__ __forceinline__ void prefetch_token(const uint16_t* q, const uint16_t* k, int64_t q_stride,
+                                               int64_t k_stride, int64_t tok, int part) {
+  if (!kVec) return;
+  const uint16_t* qrow = q + tok * q_stride;
+  if (part == 0) {
+    prefetch_row_slices<1>(k + tok * k_stride, 0);
+    prefetch_row_slices<1>(qrow + 3 * kHeadDim, 0);
+  } else {
+    prefetch_row_slices<1>(qrow + (part - 1) * kHeadDim, 0);
+    if (part < 3) prefetch_row_slices<1>(qrow + (part + 3) * kHeadDim, 0);
+  }
+}
+
 // Gathers this part's cos/sin at `pos`; false when pos is outside the cache
 // (nothing is read then).
 template <bool kVec>
@@ -313,10 +356,6 @@ enum class Source { kDense, kTileTable, kTileSlots };
 constexpr int kTableCap = 2048;  // table entries of the kTileTable source (8 KB when staged in shared memory)
 // warp_table_covers searches two levels of at most 32 x 64 entries
 static_assert(kTableCap <= 32 * 64, "the warp search covers at most 2048 table entries");
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
 
 // Starts copying tile_starts[0..n) into shared memory (4-byte cp.async; the
 // table is only 4-byte aligned).

@@ -81,6 +81,23 @@ bool head_split_shape(int64_t tokens, LaunchShape& shape) {
   return int64_t(shape.grid) * shape.block >= items;
 }
 
+// CTAs per SM of one streaming launch (rope_ordinary_stream_kernel): below the
+// five its registers allow, so part of the next launch fits beside it.
+constexpr int kStreamCtasPerSm = 4;
+
+// CTAs of a streaming launch over `items` items: warp-sized CTAs while the
+// launch is below two 128-thread CTAs per SM (so its tokens spread over every
+// SM), else one item per thread up to kStreamCtasPerSm CTAs per SM, looping
+// above that.
+LaunchShape stream_shape(int64_t items) {
+  const LaunchShape small = shape_for(items);
+  if (small.block != unsigned(kBlock)) return small;
+  const int sms = current_sm_count();
+  const int64_t need = (items + kBlock - 1) / kBlock;
+  const int64_t cap = sms > 0 ? int64_t(sms) * kStreamCtasPerSm : need;
+  return {unsigned(need < cap ? need : cap), unsigned(kBlock)};
+}
+
 // Launches carry the programmatic-stream-serialization attribute (PDL) unless
 // the environment sets WELM_ROPE_PDL=0: the grid may be scheduled while the
 // previous kernel in the stream drains, and waits in pdl_enter() before it

@@ -1,5 +1,7 @@
-// rope_ordinary.cu — ordinary prefill / decode kernel (dense, staged tile
-// table and tile slots) and its C entry welm_rope_ordinary.
+// rope_ordinary.cu — ordinary prefill / decode kernels (one head per thread
+// for small dense launches, the streaming dense kernel above that, and the
+// segmented kernel over a staged tile table or tile slots) and the C entry
+// welm_rope_ordinary.
 
 #include "rope_host.cuh"
 
@@ -33,6 +35,7 @@ __global__ void __launch_bounds__(kBlock) rope_ordinary_kernel(const RopeArgs a)
   int64_t pos_hint = -1;
   if (kSrc == Source::kTileTable) prefetch_lines(a.tile_starts, int64_t(a.num_tiles + 1) * sizeof(int32_t));
   if (kSrc != Source::kTileSlots && item0 < a.k_items) {  // tokens are items: warm the first item's row
+    prefetch_token<kVec>(a.q, a.k, a.q_stride, a.k_stride, item0 >> kPartShift, item0 & (kParts - 1));
     pos_hint = hint_load(a.positions + (item0 >> kPartShift));
     prefetch_cos_sin_row(a.cache, a.max_position, pos_hint, item0 & (kParts - 1));
   }
@@ -77,6 +80,50 @@ __global__ void __launch_bounds__(kBlock) rope_ordinary_kernel(const RopeArgs a)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Dense prefill above the one-head range (the bench workload, M = 16384).
+// One item (token, part) per thread, in CTAs small enough in registers (at
+// most 102, five CTAs per SM) that while one launch runs, a large part of the
+// next launch in the stream is already resident beside it: under programmatic
+// dependent launch the next launch's CTAs start as soon as every CTA of this
+// one has passed its dependency wait, and they use the time before their own
+// wait to ask L2 for every line their item will read — the token's rope-slice
+// lines (prefetch.global.L2), its position line (the hint load) and its
+// cos/sin lines at the hinted position.  A prefetch into L2 cannot return
+// stale data (L2 is where the previous grid's writes land), so results are
+// unchanged, but DRAM keeps streaming the next launch's reads while this one
+// drains, and after the wait its loads hit L2.  Measured on one B200 at
+// M = 16384 (graph replay, L2-cold rotating buffers, us per launch): the
+// one-wave kernel without the data prefetch 6.99; with it 6.07.  What did not
+// help: a grid of two CTAs per SM looping over items (7.6: each thread's items
+// then pay their latency chains one after another), splitting a token's seven
+// heads into two rounds to fit two whole launches per SM (7.5), 16-byte
+// cp.async reads into a shared-memory scratch slot instead of the prefetch
+// (6.6: the real reads delay the completing launch, and the static shared
+// array shrinks L1), and 4 or 6 CTAs per SM (6.4 and 8.5).
+// Launches above one item per thread (more than 4 CTAs per SM) loop, each
+// thread prefetching its next item's lines before it works on the current.
+// ---------------------------------------------------------------------------
+template <bool kVec>
+__global__ void __launch_bounds__(kBlock, 5) rope_ordinary_stream_kernel(const RopeArgs a) {
+  const int stride = gridDim.x * blockDim.x;
+  const int first = blockIdx.x * blockDim.x + threadIdx.x;
+  int64_t hint = -1;
+  if (first < a.k_items) {  // before the wait: the first item's lines
+    prefetch_token<kVec>(a.q, a.k, a.q_stride, a.k_stride, first >> kPartShift, first & (kParts - 1));
+    hint = hint_load(a.positions + (first >> kPartShift));
+    prefetch_cos_sin_row(a.cache, a.max_position, hint, first & (kParts - 1));
+  }
+  pdl_enter();
+  for (int item = first; item < a.k_items; item += stride) {
+    const int next = item + stride;
+    if (next < a.k_items)
+      prefetch_token<kVec>(a.q, a.k, a.q_stride, a.k_stride, next >> kPartShift, next & (kParts - 1));
+    ordinary_token<kVec>(a, item >> kPartShift, item & (kParts - 1), hint);
+    hint = -1;
+  }
+}
+
 // Small dense launches: one head per thread instead of seven.  Item =
 // ((token * 7 + head) * 4 + part), head 0 the K head and 1..6 the Q heads, so
 // four consecutive lanes cover one head's rope slice and a warp covers eight
@@ -91,8 +138,10 @@ __global__ void __launch_bounds__(kBlock) rope_ordinary_head_kernel(const RopeAr
   const int64_t tok = slice / kHeadsPerToken;
   const int head = slice - int(tok) * kHeadsPerToken;
   const bool live = item < a.k_items;
+  uint16_t* row = head == 0 ? a.k + tok * a.k_stride : a.q + tok * a.q_stride + (head - 1) * kHeadDim;
   int64_t pos_hint = -1;
-  if (live) {
+  if (live) {  // before the wait: the head's slice line(s), the position and the cos/sin lines
+    if (kVec && part == 0) prefetch_row_slices<1>(row, 0);
     pos_hint = hint_load(a.positions + tok);
     if (head == 0) prefetch_cos_sin_row(a.cache, a.max_position, pos_hint, part);
   }
@@ -100,7 +149,7 @@ __global__ void __launch_bounds__(kBlock) rope_ordinary_head_kernel(const RopeAr
   if (!live) return;
   const int64_t pos = __ldg(a.positions + tok);
   Slices<kVec, 1> x;
-  x.load(head == 0 ? a.k + tok * a.k_stride : a.q + tok * a.q_stride + (head - 1) * kHeadDim, part);
+  x.load(row, part);
   RowGather<kVec> g;
   g.issue(a, -1, pos_hint, part);
   if (!g.finish(a, pos, part)) {
@@ -120,9 +169,10 @@ int launch_ordinary(const Plan& plan, const RopeArgs& a, cudaStream_t s) {
       h.k_items = int32_t(items);
       return launch(rope_ordinary_head_kernel<kVec>, shape.grid, shape.block, 0, s, h);
     }
+    shape = stream_shape(plan.token_items);
+    return launch(rope_ordinary_stream_kernel<kVec>, shape.grid, shape.block, 0, s, a);
   }
   switch (plan.src) {
-    case Source::kDense: return launch_plan(rope_ordinary_kernel<kVec, Source::kDense>, plan, a, s);
     case Source::kTileTable: return launch_plan(rope_ordinary_kernel<kVec, Source::kTileTable>, plan, a, s);
     default: return launch_plan(rope_ordinary_kernel<kVec, Source::kTileSlots>, plan, a, s);
   }

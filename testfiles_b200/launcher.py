@@ -6,7 +6,8 @@
 
 ``--iters N`` launches the op N times eagerly on one buffer set with a fixed
 kernel name per path (``rope_ordinary_head_kernel`` for dense launches of at
-most 4096 tokens, else ``rope_ordinary_kernel``; ``rope_mirror_kernel``), for
+most 4096 tokens, ``rope_ordinary_stream_kernel`` for larger dense launches,
+``rope_ordinary_kernel`` for segmented ones; ``rope_mirror_kernel``), for
 ``ncu -k regex:…`` captures — the B200 analogue of the reference's msprof
 launch stub (run_welmv4_inplace_rope_prod_m16384_npu.py:1-60).
 
@@ -468,8 +469,8 @@ def kernel_name(case: workloads.Case) -> str:
     """The kernel a case's launch runs, for ``ncu -k`` filters."""
     if case.is_mirror:
         return "rope_mirror_kernel"
-    if not case.is_segmented and case.n_tokens <= HEAD_SPLIT_MAX_TOKENS:
-        return "rope_ordinary_head_kernel"
+    if not case.is_segmented:
+        return "rope_ordinary_head_kernel" if case.n_tokens <= HEAD_SPLIT_MAX_TOKENS else "rope_ordinary_stream_kernel"
     return "rope_ordinary_kernel"
 
 
