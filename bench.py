@@ -139,15 +139,20 @@ def hbm_peak() -> tuple[float, str]:
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def profiled_traffic() -> int | None:
-    """DRAM bytes per launch (read + write) from the committed ncu summary."""
+def profiled_traffic() -> tuple[int | None, str]:
+    """DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum of
+    one ncu capture of the bench kernel) as recorded in the committed profile
+    summary, and where the figure comes from.  A bench run cannot profile
+    itself, so the figure is the last capture's, not this run's."""
     try:
         for line in PROFILE_SUMMARY.read_text().splitlines():
             if line.strip().startswith("traffic_bytes_per_launch:"):
-                return int(float(line.split(":", 1)[1].strip().split()[0]))
+                value = int(float(line.split(":", 1)[1].strip().split()[0]))
+                return value, (f"profile summary {PROFILE_SUMMARY.relative_to(REPO)} (ncu dram__bytes_read.sum + "
+                               "dram__bytes_write.sum of one launch, captured separately; not measured by this run)")
     except Exception:  # noqa: BLE001
-        return None
-    return None
+        return None, "no profile summary"
+    return None, "no traffic line in the profile summary"
 
 
 # ---------------------------------------------------------------------------
@@ -304,7 +309,9 @@ def run_b200_arm(args) -> int:
 
         # Capture the timed launches: `body` holds GRAPH_LAUNCHES launches
         # cycling through the buffer sets, `tail` the remainder, so exactly
-        # K launches run in the timed region.
+        # K launches run in the timed region.  Every graph that the timed
+        # region replays is itself replayed three times first, so no first
+        # replay (graph upload, cold instruction caches) is timed.
         def capture(count: int):
             if count == 0:
                 return None
@@ -314,18 +321,26 @@ def run_b200_arm(args) -> int:
                     step(i)
             return g
 
-        body = capture(GRAPH_LAUNCHES)
         reps, rem = divmod(args.steps, GRAPH_LAUNCHES)
+        body = capture(GRAPH_LAUNCHES) if reps else None
         tail = capture(rem)
         for _ in range(3):
-            body.replay()
+            for g in (body, tail):
+                if g is not None:
+                    g.replay()
         torch.cuda.synchronize(device)
 
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier(dist, device)
+        # ~100 us of device-side delay ahead of the start event, so the host
+        # has submitted the graphs before timing begins (a short timed region
+        # would otherwise include the submission latency); the first timed
+        # launch still starts cold, with no previous launch of the op to
+        # overlap with
+        torch.cuda._sleep(200_000)
         start.record(stream)
         for _ in range(reps):
-            body.replay()
+            body.replay()  # reps > 0 only when body was captured
         if tail is not None:
             tail.replay()
         end.record(stream)
@@ -401,6 +416,7 @@ def run_b200_arm(args) -> int:
     full_per_step = full_ms / 1e3 / e2e_steps
     staged_per_step = staged_ms / 1e3 / e2e_steps
     h2d, d2h = welm_host.lane_bytes(TOKENS)
+    traffic, traffic_source = profiled_traffic()
 
     line = None
     if rank == 0:
@@ -445,21 +461,23 @@ def run_b200_arm(args) -> int:
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                 else "fallback 6.65 TB/s",
                 "frac_of_8tbs_spec": round(per_launch_gbs / 8000.0, 4),
-                "traffic": profiled_traffic(),
+                "traffic": traffic,
+                "traffic_source": traffic_source,
                 "same_size_copy_us": round(copy_ms * 1e3, 3),
                 "frac_of_same_size_copy": round(copy_ms * 1e3 / (per_step_s * 1e6), 4),
                 "same_size_copy": "torch copy_ of 16.8 MB (33.7 MB of traffic) per step, graph-replayed over "
                                   "8 rotating buffer pairs like the op: the practical ceiling at this size",
                 "stream_copy_us": round(stream_copy_us, 3),
                 "frac_of_stream_copy": round(stream_copy_us / (per_step_s * 1e6), 4),
-                "stream_copy": "the library's streaming copy kernel (welm_rope_ceiling_copy: one 16-byte vector "
-                               "per thread, PDL) on the same bytes and buffer rotation",
+                "stream_copy": "the library's streaming copy kernel (welm_rope_ceiling_copy, PDL) on the same "
+                               "bytes and buffer rotation: one 16-byte vector per thread up to a full-occupancy "
+                               "wave, four per thread above (this size is above)",
                 "slice_floor_us": round(slice_floor_us, 3),
                 "frac_of_slice_floor": round(slice_floor_us / (per_step_s * 1e6), 4),
                 "slice_floor": "welm_rope_ceiling_slices on the op's own buffers: the same launch shape, loads "
                                "and stores of the rope slices, without the position / cos-sin gather and "
                                "the arithmetic",
-                "kernel": "rope_ordinary_kernel<vec,contiguous>",
+                "kernel": "rope_ordinary_stream_kernel<vec=1> (one item per thread, pre-wait L2 prefetch)",
                 "bytes_per_launch": algorithmic_bytes(TOKENS),
             },
             "cpu_baseline": cpu,

@@ -26,10 +26,12 @@ def test_algorithmic_bytes_match_the_workload_model():
 
 def test_traffic_figure_comes_from_the_committed_profile():
     bench = load_bench()
-    traffic = bench.profiled_traffic()
+    traffic, source = bench.profiled_traffic()
     assert traffic is not None
     # DRAM bytes per launch close to the algorithmic reads (writes stay in L2)
     assert 19_000_000 <= traffic <= 19_100_000
+    # the line says where the figure comes from: a separate capture, not this run
+    assert "profiles/rope_ordinary_prefill_m16384.md" in source and "not measured by this run" in source
 
 
 def test_vs_baseline_uses_the_published_figure():
