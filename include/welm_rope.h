@@ -239,7 +239,10 @@ int welm_rope_copy_rope_lanes(void* dst, const void* src, int64_t rows, int64_t 
  *
  * The first call on each device looks up the staging area's device address
  * (cudaGetSymbolAddress, with that device current); make that first call
- * before any stream capture.  Every call shares the one staging area: calls
+ * before any stream capture.  The address is kept for the life of the
+ * process, so do not use this entry after a cudaDeviceReset of that device
+ * (the reset unloads the library's device code and the kept address may no
+ * longer be mapped).  Every call shares the one staging area: calls
  * whose work overlaps on the GPU (different streams, or different host
  * threads without ordering) race on it and must be serialised by the caller.
  * The area is fully rewritten by each call before it is read, so the previous
