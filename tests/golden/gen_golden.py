@@ -1,9 +1,10 @@
 #!/usr/bin/env python3
 """Generate the golden fixtures from the reference's OWN Python code.
 
-Run in a container where the reference source tree is available:
+Run where the reference source tree is available, naming its directory
+(or set WELM_ROPE_REFERENCE_DIR):
 
-    python tests/golden/gen_golden.py --reference /root/reference
+    python tests/golden/gen_golden.py --reference <reference checkout>
 
 It imports ``bench_welmv4_inplace_rope_npu`` with an empty stand-in for the
 Ascend-only ``torch_npu`` module (nothing of that module is used by the
@@ -26,6 +27,7 @@ their digests, and compare output digests.
 from __future__ import annotations
 
 import argparse
+import os
 import hashlib
 import json
 import platform
@@ -58,8 +60,11 @@ def load_reference(path: Path):
 
 def main() -> int:
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", default=os.environ.get("WELM_ROPE_REFERENCE_DIR"),
+                        help="directory of the reference checkout (default: $WELM_ROPE_REFERENCE_DIR)")
     args = parser.parse_args()
+    if not args.reference:
+        parser.error("name the reference checkout with --reference or WELM_ROPE_REFERENCE_DIR")
     torch.set_num_threads(max(1, torch.get_num_threads()))
     ref = load_reference(Path(args.reference))
     sys.path.insert(0, str(REPO))
