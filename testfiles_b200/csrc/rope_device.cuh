@@ -66,7 +66,7 @@ struct RopeArgs {
   int64_t n_tokens;            // K rows / positions length
   int64_t max_position;        // cache rows
   int32_t* status;             // optional device status word
-  int32_t q_items;             // Q-row items (mirror): BS * kParts
+  int32_t q_items;             // Q items (mirror): BS * kParts, or BS * 6 * kParts one head per item
   int32_t k_items;             // token items: tokens (or tile slots) * kParts
   int32_t num_tiles;           // work tiles (segmented)
 };
@@ -341,21 +341,20 @@ struct RowGather {
 // (bench_welmv4_inplace_rope_npu.py:700-718, 856-867): tile i covers
 // [starts[i], starts[i] + min(64, starts[i+1] - starts[i])).
 //   kDense:     has_segments = 0; token = slot, slots = min(N, 64 * tiles).
-//   kTileTable: has_segments = 1 with at most kTableCap table entries;
-//               items are tokens 0..N-1 in order, so every load is issued at
-//               once, and a token is rotated iff a tile covers it (ordinary:
-//               binary search of the table staged in shared memory; mirror:
-//               a warp-cooperative search of the global table while the
-//               loads fly).  Exact for any non-decreasing table; other tables
-//               are flagged.
-//   kTileSlots: has_segments = 1 with a large table; 64 slots per tile,
-//               token = starts[tile] + slot (one extra dependent load).
+//   kTileTable: (ordinary) has_segments = 1 with at most kTableCap table
+//               entries; items are tokens 0..N-1 in order, so every load is
+//               issued at once, and a token is rotated iff a tile covers it
+//               (binary search of the table staged in shared memory).  Exact
+//               for any non-decreasing table; other tables are flagged.
+//   kTileSlots: has_segments = 1; 64 slots per tile, token = starts[tile] +
+//               slot (one extra dependent load).  The ordinary kernel uses it
+//               for large tables, the mirror for every table.  A table whose
+//               tiles overlap (not non-decreasing, flagged) may reach a token
+//               from two slots.
 // ---------------------------------------------------------------------------
 enum class Source { kDense, kTileTable, kTileSlots };
 
 constexpr int kTableCap = 2048;  // table entries of the kTileTable source (8 KB when staged in shared memory)
-// warp_table_covers searches two levels of at most 32 x 64 entries
-static_assert(kTableCap <= 32 * 64, "the warp search covers at most 2048 table entries");
 
 // Starts copying tile_starts[0..n) into shared memory (4-byte cp.async; the
 // table is only 4-byte aligned).
@@ -384,31 +383,11 @@ __device__ __forceinline__ bool table_covers(const int32_t* s_tab, int num_tiles
   return i >= 0 && i < num_tiles && t - s_tab[i] < kTile;
 }
 
-// Warp-cooperative coverage test on the global tile table (read-only path;
-// its lines were prefetched into L2 in the PDL window and are read only after
-// the wait): a 32-way ballot search finds the last entry at or before the
-// warp's first token t_ref in two rounds of parallel loads (instead of
-// log2(T) dependent ones), then each lane steps forward to its own token
-// t >= t_ref.  Same answer as table_covers for every non-decreasing table;
-// for other tables (flagged by the check items) the answer is arbitrary, but
-// every index read stays in [0, num_tiles].  All 32 lanes must call it.
-__device__ __forceinline__ bool warp_table_covers(const int32_t* g_tab, int num_tiles, int64_t t_ref, int64_t t) {
-  constexpr unsigned kAll = 0xffffffffu;
-  const int lane = threadIdx.x & 31;
-  const int entries = num_tiles + 1;
-  const int stride = (entries + 31) >> 5;
-  const int e0 = lane * stride;
-  const int blocks = __popc(__ballot_sync(kAll, e0 < entries && __ldg(g_tab + e0) <= t_ref));
-  int i = -1;
-  if (blocks > 0) {  // warp-uniform
-    const int base = (blocks - 1) * stride;
-    const int e1 = base + lane, e2 = base + 32 + lane;
-    const bool le1 = lane < stride && e1 < entries && __ldg(g_tab + e1) <= t_ref;
-    const bool le2 = 32 + lane < stride && e2 < entries && __ldg(g_tab + e2) <= t_ref;
-    i = base + __popc(__ballot_sync(kAll, le1)) + __popc(__ballot_sync(kAll, le2)) - 1;
-  }
-  while (i < num_tiles && __ldg(g_tab + i + 1) <= t) ++i;
-  return i >= 0 && i < num_tiles && t - __ldg(g_tab + i) < kTile;
+// Reads a 32-bit value as a hint before the dependency wait (see hint_load).
+__device__ __forceinline__ int32_t hint_load_s32(const int32_t* p) {
+  int32_t v;
+  asm volatile("ld.global.cg.s32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
 }
 
 // Tile validation item: flags a tile that starts below 0, ends past N, runs

@@ -149,7 +149,7 @@ Plan plan_tokens(int64_t has_segments, int64_t num_work_tiles, int64_t n_tokens)
 }
 
 template <typename Kernel>
-int launch_plan(Kernel kernel, const Plan& plan, const RopeArgs& a, cudaStream_t stream, bool staged_table = true) {
+int launch_plan(Kernel kernel, const Plan& plan, const RopeArgs& a, cudaStream_t stream) {
   const int64_t total = int64_t(a.q_items) + plan.token_items + plan.check_items;
   if (plan.src == Source::kTileTable) {
     // One item per thread.  Up to one 128-thread CTA's worth of items per SM
@@ -157,7 +157,7 @@ int launch_plan(Kernel kernel, const Plan& plan, const RopeArgs& a, cudaStream_t
     // of leaving most with one CTA.  Measured on one B200 (graph replay, us):
     // segmented prefill M=4096 (8 requests) 3.55 -> 3.23; at M=8192 (32
     // requests, above this limit) warp-sized CTAs were slower, 4.43 -> 4.66.
-    const size_t smem = staged_table ? (size_t(a.num_tiles + 1) * sizeof(int32_t) + 15) & ~size_t(15) : 0;
+    const size_t smem = (size_t(a.num_tiles + 1) * sizeof(int32_t) + 15) & ~size_t(15);
     const int sms = current_sm_count();
     if (sms > 0 && total <= int64_t(sms) * kBlock)
       return launch(kernel, unsigned((total + 31) / 32), 32u, smem, stream, a);

@@ -1,19 +1,17 @@
-// rope_mirror.cu — KV-mirror kernels (tile-table / slot / dense sources, and
-// the variant driven by request lengths) and their C entries.
+// rope_mirror.cu — KV-mirror kernels (one head per item over dense tokens or
+// tile slots, and the variant driven by request lengths) and their C entries.
 
 #include "rope_host.cuh"
 
 namespace {
 
-// ---------------------------------------------------------------------------
-// KV-mirror prefill.  Items [0, q_items) are the BS Q rows (6 heads at
-// positions[last_index[b]], bench_welmv4_inplace_rope_npu.py:839-854); the
-// next k_items are K tokens (1 head at positions[t],
-// bench_welmv4_inplace_rope_npu.py:856-919).  Q rows and K rows are disjoint
-// tensors, so the two phases need no ordering.  A Q row's data loads are
-// issued before its last_index -> position -> cache chain.
-// ---------------------------------------------------------------------------
-// g has been issued (with or without hints) before src is known.
+// KV-mirror semantics: the BS Q rows are rotated at positions[last_index[b]]
+// (bench_welmv4_inplace_rope_npu.py:839-854), K token t at positions[t]
+// (bench_welmv4_inplace_rope_npu.py:856-919).  Q rows and K rows are disjoint
+// tensors, so the two phases need no ordering.
+//
+// Finishes a six-head Q row whose gather g was issued (with or without hints)
+// before src was known.
 template <bool kVec>
 __device__ __forceinline__ void finish_q_row(const RopeArgs& a, Slices<kVec, kQHeads>& qx, int64_t src,
                                              RowGather<kVec>& g, int part) {
@@ -28,97 +26,94 @@ __device__ __forceinline__ void finish_q_row(const RopeArgs& a, Slices<kVec, kQH
   qx.rotate_store(g.cs);
 }
 
-template <bool kVec>
-__device__ __forceinline__ void mirror_q_row(const RopeArgs& a, int b, int part, int64_t src_hint,
-                                             int64_t pos_hint) {
-  Slices<kVec, kQHeads> qx;
-  qx.load(a.q + int64_t(b) * a.q_stride, part);
-  const int64_t src = __ldg(a.last_index + b);
-  RowGather<kVec> g;
-  g.issue(a, src_hint, pos_hint, part);
-  finish_q_row<kVec>(a, qx, src, g, part);
-}
-
-template <bool kVec>
-__device__ __forceinline__ void mirror_k_token(const RopeArgs& a, int64_t tok, int part, int64_t pos_hint) {
-  const int64_t pos = __ldg(a.positions + tok);
-  Slices<kVec, 1> kx;
-  kx.load(a.k + tok * a.k_stride, part);
-  RowGather<kVec> g;
-  g.issue(a, -1, pos_hint, part);
-  if (!g.finish(a, pos, part)) {
-    if (part == 0) raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
-    return;
-  }
-  kx.rotate_store(g.cs);
-}
-
-// At most 128 registers: 4 CTAs per SM keep a 16384-token launch in one wave.
+// ---------------------------------------------------------------------------
+// KV-mirror prefill, one head per item.  Items [0, q_items) are Q heads, item
+// = (row * 6 + head) * 4 + part.  The K items follow: with has_segments = 0
+// one per (token, part); with a tile table one per (tile, slot, part), 64
+// slots per tile, slot j of tile i holding token starts[i] + j when j <
+// min(64, starts[i+1] - starts[i]) (bench_welmv4_inplace_rope_npu.py:856-867),
+// so no token-to-tile search is needed.  Every thread holds one head's two
+// 16-byte vectors and its cos/sin (at most 64 registers), so under
+// programmatic dependent launch most or all of the next launch's CTAs are
+// resident while this one runs, and before their dependency wait each item
+// does what needs none of the previous launch's results:
+//   * reads as hints its token's position (Q heads: last_index, then the
+//     position it names; slots: starts[i], then the position of the token it
+//     gives), prefetching the slice line and the cos/sin lines they name.
+// After the wait one round of loads finishes an item in the common case: the
+// data and position at the hinted token next to the real table entries (or
+// last_index), and cos/sin at the hinted position (RowGather).  An item keeps
+// what it loaded on hints only when the real chain names the same token and
+// position; otherwise it reloads, so results equal the plain dependent
+// chain's for every input.
+// ---------------------------------------------------------------------------
 template <bool kVec, Source kSrc>
-__global__ void __launch_bounds__(kBlock, 4) rope_mirror_kernel(const RopeArgs a) {
-  // warm the first item's cos/sin row (Q rows: through a last_index hint)
-  const int item0 = blockIdx.x * blockDim.x + threadIdx.x;
-  int64_t src_hint = -1, pos_hint = -1;
-  if (kSrc == Source::kTileTable) prefetch_lines(a.tile_starts, int64_t(a.num_tiles + 1) * sizeof(int32_t));
-  if (item0 < a.q_items) {
-    src_hint = hint_load(a.last_index + (item0 >> kPartShift));
+__global__ void __launch_bounds__(kBlock, 8) rope_mirror_head_kernel(const RopeArgs a) {
+  static_assert(kSrc == Source::kDense || kSrc == Source::kTileSlots, "dense or slot items");
+  const int item = blockIdx.x * blockDim.x + threadIdx.x;
+  const int part = item & (kParts - 1);
+  const bool is_q = item < a.q_items;
+  const int k_item = item - a.q_items;
+  const bool is_k = !is_q && k_item < a.k_items;
+  const int q_slice = is_q ? (item >> kPartShift) : 0;
+  const int row = q_slice / kQHeads;
+  const int head = q_slice - row * kQHeads;
+  const int slot = k_item >> kPartShift;
+
+  // Before the wait: hints and prefetches only.
+  int64_t src_hint = -1, pos_hint = -1, tok_hint = -1;
+  uint16_t* q_row = a.q + int64_t(row) * a.q_stride + head * kHeadDim;
+  if (is_q) {
+    if (kVec && part == 0) prefetch_row_slices<1>(q_row, 0);
+    src_hint = hint_load(a.last_index + row);
     if (src_hint >= 0 && src_hint < a.n_tokens) pos_hint = hint_load(a.positions + src_hint);
-  } else if (kSrc != Source::kTileSlots && item0 - a.q_items < a.k_items) {
-    pos_hint = hint_load(a.positions + ((item0 - a.q_items) >> kPartShift));
-  }
-  prefetch_cos_sin_row(a.cache, a.max_position, pos_hint, item0 & (kParts - 1));
-  pdl_enter();
-  if constexpr (kSrc == Source::kTileTable) {
-    // One item per thread: Q rows, then tokens [0, k_items / 4), then one
-    // check per tile.  Phase 1 issues the loads of whatever item the thread
-    // owns; the coverage search (warp-uniform, no barrier) runs while they
-    // fly; phase 2 finishes the item.
-    const int item = blockIdx.x * blockDim.x + threadIdx.x;
-    const int part = item & (kParts - 1);
-    const bool is_q = item < a.q_items;
-    const int k_item = item - a.q_items;
-    const bool is_token = !is_q && k_item < a.k_items;
-    const int64_t tok = is_token ? (k_item >> kPartShift) : 0;
-    Slices<kVec, kQHeads> qx;
-    Slices<kVec, 1> kx;
-    RowGather<kVec> g;
-    int64_t src = 0, pos = 0;
-    if (is_q) {
-      qx.load(a.q + int64_t(item >> kPartShift) * a.q_stride, part);
-      src = __ldg(a.last_index + (item >> kPartShift));
-      g.issue(a, src_hint, pos_hint, part);
-    } else if (is_token) {
-      pos = __ldg(a.positions + tok);
-      kx.load(a.k + tok * a.k_stride, part);
-      g.issue(a, -1, pos_hint, part);
-    } else if (k_item - a.k_items < a.num_tiles) {
-      check_tile(a, k_item - a.k_items);
+  } else if (is_k) {
+    if (kSrc == Source::kDense) {
+      tok_hint = slot;
+    } else {
+      const int tile = slot / kTile, j = slot - tile * kTile;
+      const int64_t b = hint_load_s32(a.tile_starts + tile), e = hint_load_s32(a.tile_starts + tile + 1);
+      if (j < e - b && j < kTile && b + j >= 0 && b + j < a.n_tokens) tok_hint = b + j;
     }
-    // the coverage search runs while the loads above are in flight
-    const int first_k = max(item & ~31, a.q_items) - a.q_items;  // the warp's first K item
-    const int64_t t_ref = first_k < a.k_items ? int64_t(first_k >> kPartShift) : 0;
-    const bool covered = warp_table_covers(a.tile_starts, a.num_tiles, t_ref, is_token ? tok : t_ref);
-    if (is_q) {
-      finish_q_row<kVec>(a, qx, src, g, part);
-    } else if (is_token && covered) {
+    if (tok_hint >= 0) {
+      if (kVec && part == 0) prefetch_row_slices<1>(a.k + tok_hint * a.k_stride, 0);
+      pos_hint = hint_load(a.positions + tok_hint);
+    }
+  }
+  prefetch_cos_sin_row(a.cache, a.max_position, pos_hint, part);
+  pdl_enter();
+
+  Slices<kVec, 1> x;
+  RowGather<kVec> g;
+  if (is_q) {
+    x.load(q_row, part);
+    const int64_t src = __ldg(a.last_index + row);
+    g.issue(a, src_hint, pos_hint, part);
+    const bool flag = part == 0 && head == 0;  // one report per row
+    if (src < 0 || src >= a.n_tokens) {
+      if (flag) raise_status(a.status, WELM_ROPE_DEV_BAD_LAST_INDEX);
+    } else if (!g.finish(a, g.position(a, src), part)) {
+      if (flag) raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
+    } else {
+      x.rotate_store(g.cs);
+    }
+  } else if (is_k) {
+    int64_t pos = 0;
+    if (tok_hint >= 0) {  // loads on the hinted token (after the wait: current data)
+      x.load(a.k + tok_hint * a.k_stride, part);
+      pos = __ldg(a.positions + tok_hint);
+    }
+    g.issue(a, -1, pos_hint, part);
+    int64_t tok;
+    if (slot_token<kSrc>(a, slot, part, tok)) {  // the real token (slots: the real table entries)
+      if (tok != tok_hint) {
+        x.load(a.k + tok * a.k_stride, part);
+        pos = __ldg(a.positions + tok);
+      }
       if (g.finish(a, pos, part)) {
-        kx.rotate_store(g.cs);
+        x.rotate_store(g.cs);
       } else if (part == 0) {
         raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
-      }
-    }
-  } else {
-    const int stride = gridDim.x * blockDim.x;
-    const int total = a.q_items + a.k_items;
-    for (int item = blockIdx.x * blockDim.x + threadIdx.x; item < total; item += stride) {
-      const int part = item & (kParts - 1);
-      const bool first = item == item0;
-      if (item < a.q_items) {
-        mirror_q_row<kVec>(a, item >> kPartShift, part, first ? src_hint : -1, first ? pos_hint : -1);
-      } else {
-        int64_t tok;
-        if (slot_token<kSrc>(a, (item - a.q_items) >> kPartShift, part, tok))
-          mirror_k_token<kVec>(a, tok, part, first ? pos_hint : -1);
       }
     }
   }
@@ -239,13 +234,25 @@ __global__ void __launch_bounds__(kBlock, 4) rope_mirror_lens_kernel(const RopeA
   if (negative && blockIdx.x == 0 && threadIdx.x == 0) raise_status(a.status, WELM_ROPE_DEV_BAD_LENGTH);
 }
 
+// Launch of the one-head kernel: one item per thread, in warp-sized CTAs while
+// the launch is below one 128-thread CTA per SM (its items then spread over
+// every SM), else in 128-thread CTAs.
+template <typename Kernel>
+int launch_heads(Kernel kernel, int64_t total, const RopeArgs& a, cudaStream_t s) {
+  const int sms = current_sm_count();
+  if (sms > 0 && total <= int64_t(sms) * kBlock) return launch(kernel, unsigned((total + 31) / 32), 32u, 0, s, a);
+  return launch(kernel, unsigned((total + kBlock - 1) / kBlock), kBlock, 0, s, a);
+}
+
 template <bool kVec>
-int launch_mirror(const Plan& plan, const RopeArgs& a, cudaStream_t s) {
-  switch (plan.src) {
-    case Source::kDense: return launch_plan(rope_mirror_kernel<kVec, Source::kDense>, plan, a, s);
-    case Source::kTileTable: return launch_plan(rope_mirror_kernel<kVec, Source::kTileTable>, plan, a, s, false);
-    default: return launch_plan(rope_mirror_kernel<kVec, Source::kTileSlots>, plan, a, s);
-  }
+int launch_mirror(const Plan& plan, const RopeArgs& a, int64_t rows, cudaStream_t s) {
+  RopeArgs h = a;
+  h.q_items = int32_t(rows * kQHeads * kParts);
+  if (plan.src == Source::kDense)
+    return launch_heads(rope_mirror_head_kernel<kVec, Source::kDense>, int64_t(h.q_items) + plan.token_items, h, s);
+  // tile slots for every table size: 64 slots per tile
+  h.k_items = int32_t(int64_t(a.num_tiles) * kTile * kParts);
+  return launch_heads(rope_mirror_head_kernel<kVec, Source::kTileSlots>, int64_t(h.q_items) + h.k_items, h, s);
 }
 
 }  // namespace
@@ -265,7 +272,8 @@ int welm_rope_mirror(void* q, void* k, const int64_t* positions, const float* co
     return WELM_ROPE_ERR_BAD_SIZE;
   const Plan plan = n_tokens > 0 ? plan_tokens(has_segments, num_work_tiles, n_tokens) : Plan{Source::kDense, 0, 0};
   const int64_t rows = n_tokens > 0 ? batch_size : 0;  // Q rows need a valid last_index target
-  if (rows * kParts + plan.token_items + plan.check_items > kMaxItems) return WELM_ROPE_ERR_BAD_SIZE;
+  const int64_t k_items = has_segments ? num_work_tiles * kTile * kParts : plan.token_items;
+  if (rows * kQHeads * kParts + k_items > kMaxItems) return WELM_ROPE_ERR_BAD_SIZE;
   if (plan.token_items == 0 && rows == 0) return WELM_ROPE_OK;
   if (!positions || !cos_sin_cache) return WELM_ROPE_ERR_NULL_POINTER;
   if (rows > 0 && (!q || !last_index)) return WELM_ROPE_ERR_NULL_POINTER;
@@ -293,7 +301,7 @@ int welm_rope_mirror(void* q, void* k, const int64_t* positions, const float* co
                    (rows <= 1 || q_token_stride % 8 == 0) &&
                    (n_tokens <= 1 || k_token_stride % 8 == 0);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  return vec ? launch_mirror<true>(plan, a, s) : launch_mirror<false>(plan, a, s);
+  return vec ? launch_mirror<true>(plan, a, rows, s) : launch_mirror<false>(plan, a, rows, s);
 }
 
 int welm_rope_mirror_from_lens(void* q, void* k, const int64_t* positions, const float* cos_sin_cache,
