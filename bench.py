@@ -189,9 +189,14 @@ def run_reference_arm(args) -> int:
     sample = int(min(TOKENS, max(64, TOKENS * budget / full[0])) // 64 * 64)
     part = workloads.Inputs(inputs.query[:sample], inputs.key[:sample], inputs.positions[:sample], inputs.cache)
     times, threads = cpu_reference_time(part, runs=args.steps, warmup=max(0, args.warmup))
-    per_step = statistics.mean(times)
-    gbs = algorithmic_bytes(sample) / per_step / 1e9
-    per_launch_us = per_step * 1e6 * TOKENS / sample
+    per_sample = statistics.mean(times)
+    gbs = algorithmic_bytes(sample) / per_sample / 1e9
+    # The workload is the GPU arm's at this N: world requests of 16384 tokens
+    # (one per GPU there); the CPU path runs them one after another on this
+    # host, so a step of the global batch takes world x 16384 / sample times
+    # the sample's time, and the rate (GB/s) is the sample's.
+    global_tokens = TOKENS * world
+    per_step = per_sample * global_tokens / sample
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -201,18 +206,20 @@ def run_reference_arm(args) -> int:
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": round(per_step * 1e3, 4),
-        "us_per_launch": round(per_launch_us, 2),
+        "us_per_launch": round(per_sample * 1e6 * TOKENS / sample, 2),
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": round(gbs / PUBLISHED_GBS, 4),
         "vs_baseline_source": PUBLISHED_SOURCE,
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) bf16 Q/K, positions 0..M-1)",
-        "config": workload_config(1),
+        "config": workload_config(world),
         "cpu_baseline": {
             "value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"first {sample} of 16384 tokens per step (reference torch CPU path restated), "
-                      f"{args.steps} steps after {args.warmup} warm-up, mean; us_per_launch scaled to M=16384",
+            "sample": f"first {sample} of the 16384 tokens of one request per step (reference torch CPU path "
+                      f"restated), {args.steps} steps after {args.warmup} warm-up, mean; the global batch of "
+                      f"{world} request(s) runs at this rate on this host's cores, so ms_per_step is "
+                      f"{global_tokens} / {sample} sample times; us_per_launch is one 16384-token request",
         },
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -236,6 +243,202 @@ def timed_steps(step, count: int, dist, device, stream) -> float:
     end.record(stream)
     barrier(dist, device)
     return max_over_ranks(dist, start.elapsed_time(end), device)
+
+
+# ---------------------------------------------------------------------------
+# Result checks of the GPU arm: after timing, each leg runs once more on
+# pristine inputs; rank 0 gathers every rank's rows (NCCL all_gather when N > 1)
+# and compares their SHA-256 with the digest of the reference's own outputs
+# for that configuration, recorded by tests/golden/gen_golden.py.
+# ---------------------------------------------------------------------------
+GOLDEN_OUTPUTS = REPO / "tests" / "golden" / "golden_outputs.json"
+L2_BYTES = 126 * 1024 * 1024
+MIRROR_CASE = "b_mirror_segmented_n16384_bs128_uneven"
+PREFILL_CASE = "b_prefill_m16384"
+
+
+def sha256_rows(t: torch.Tensor) -> str:
+    """SHA-256 of a tensor's bytes, bf16 taken as int16 (the fixtures' rule)."""
+    import hashlib
+
+    t = t.detach().contiguous().cpu()
+    if t.dtype == torch.bfloat16:
+        t = t.view(torch.int16)
+    return hashlib.sha256(t.numpy().tobytes()).hexdigest()
+
+
+def golden_outputs(case_name: str) -> dict | None:
+    try:
+        return json.loads(GOLDEN_OUTPUTS.read_text())["cases"][case_name]["outputs"]
+    except Exception:  # noqa: BLE001
+        return None
+
+
+def gather_rows(dist, t: torch.Tensor, counts: list[int]) -> torch.Tensor | None:
+    if dist is None:
+        return t
+    from testfiles_b200 import sharding
+
+    return sharding.gather_rows(t, counts)
+
+
+def parity_record(dist, rank: int, q: torch.Tensor, k: torch.Tensor, q_counts: list[int], k_counts: list[int],
+                  case_name: str, copies: int = 1) -> dict | None:
+    """Gathers Q and K rows to rank 0 and compares them with the golden
+    digests of `case_name` (`copies` identical requests laid end to end)."""
+    q_all = gather_rows(dist, q, q_counts)
+    k_all = gather_rows(dist, k, k_counts)
+    if rank != 0:
+        return None
+    want = golden_outputs(case_name)
+    if want is None:
+        return {"bit_exact": None, "reason": f"no golden digest for {case_name}"}
+    ok = True
+    for qc, kc in zip(q_all.chunk(copies), k_all.chunk(copies)):
+        ok &= sha256_rows(qc) == want["query"] and sha256_rows(kc) == want["key"]
+    return {
+        "bit_exact": bool(ok),
+        # equal digests mean equal bits: no lane differs (0 ulp, lanes 0..191 untouched)
+        "max_abs_q": 0.0 if ok else None,
+        "max_abs_k": 0.0 if ok else None,
+        "max_ulp": 0 if ok else None,
+        "rows_checked": {"query": int(q_all.shape[0]), "key": int(k_all.shape[0])},
+        "compared_with": f"SHA-256 of the reference's own outputs for {case_name} "
+                         f"({GOLDEN_OUTPUTS.relative_to(REPO)}), per request",
+        "gathered": "NCCL all_gather to rank 0" if dist is not None else "single rank",
+    }
+
+
+def replay_leg_us(launches: list, dist, device, stream, graph_launches: int = 64, replays: int = 8) -> float:
+    """Max-over-ranks µs per launch of `launches` (one callable per buffer
+    set, used in rotation), replayed from a warmed CUDA graph."""
+    for f in launches[:3]:
+        f()
+    torch.cuda.synchronize(device)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(graph_launches):
+            launches[i % len(launches)]()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(dist, device)
+    torch.cuda._sleep(200_000)
+    start.record(stream)
+    for _ in range(replays):
+        g.replay()
+    end.record(stream)
+    barrier(dist, device)
+    ms = max_over_ranks(dist, start.elapsed_time(end), device)
+    del g
+    return ms * 1e3 / (replays * graph_launches)
+
+
+def sets_for(nbytes: int) -> int:
+    """Buffer sets so that more than 2 x L2 of algorithmic bytes lie between reuses."""
+    return int(min(64, max(2, -(-2 * L2_BYTES // max(nbytes, 1)))))
+
+
+def strong_prefill_leg(dist, rank: int, world: int, device, stream, peak: float) -> dict:
+    """The headline's single M=16384 request split over the ranks in
+    64-aligned token ranges (strong scaling): value = its algorithmic bytes
+    over the slowest rank's µs per launch."""
+    import testfiles_b200 as welm
+    from testfiles_b200 import sharding, workloads
+
+    case = workloads.find_case(PREFILL_CASE)
+    host = workloads.make_inputs(case, "cpu")
+    ranges = [sharding.shard_tokens(TOKENS, world, r) for r in range(world)]
+    t0, t1 = ranges[rank]
+    local = workloads.Inputs(host.query[t0:t1], host.key[t0:t1], host.positions[t0:t1], host.cache)
+    sets = [local.to(device) for _ in range(sets_for(algorithmic_bytes(t1 - t0)))]
+    us = replay_leg_us([lambda b=b: welm.welmv4_inplace_rope_npu(b.query, b.key, b.positions, b.cache)
+                        for b in sets], dist, device, stream)
+    del sets
+    fresh = local.to(device)
+    welm.welmv4_inplace_rope_npu(fresh.query, fresh.key, fresh.positions, fresh.cache)
+    counts = [b - a for a, b in ranges]
+    check = parity_record(dist, rank, fresh.query, fresh.key, counts, counts, PREFILL_CASE)
+    gbs = algorithmic_bytes(TOKENS) / (us * 1e3)
+    return {
+        "workload": "ordinary prefill M=16384 (one request) split over the GPUs in 64-aligned token ranges",
+        "scaling": "strong", "tokens_per_gpu": counts, "us_per_launch": round(us, 3),
+        "value": round(gbs, 2), "unit": "GB/s", "tokens_per_s": round(TOKENS / (us * 1e-6), 1),
+        "frac_of_n_gpu_peak": round(gbs / (peak * world), 4), "parity": check,
+    }
+
+
+def mirror_sharded_leg(dist, rank: int, world: int, device, stream, peak: float) -> dict:
+    """The segmented KV mirror N=16384, BS=128 seeded-uneven requests, split
+    over the ranks by whole requests balanced by tokens: each rank rotates its
+    K rows and its requests' Q rows with last_index rebased to its first token
+    and a tile table rebuilt from its own requests.  value = the global
+    algorithmic bytes over the slowest rank's µs per launch."""
+    import testfiles_b200 as welm
+    from testfiles_b200 import sharding, workloads
+
+    case = workloads.find_case(MIRROR_CASE)
+    full = workloads.make_inputs(case, "cpu")
+    lens = case.segment_lens
+    ranges = sharding.shard_requests(lens, world)
+    batches = [sharding.local_batch(lens, rr, full.last_index.tolist()) for rr in ranges]
+    mine = batches[rank]
+    r0, r1 = ranges[rank]
+
+    def local_bytes(b) -> int:
+        return 520 * b.n_tokens + 1544 * (b.request_end - b.request_begin) + 4 * len(b.tile_starts)
+
+    local = workloads.Inputs(full.query[r0:r1], full.key[mine.token_begin:mine.token_end],
+                             full.positions[mine.token_begin:mine.token_end], full.cache,
+                             torch.tensor(mine.last_index, dtype=torch.int64),
+                             torch.tensor(mine.tile_starts, dtype=torch.int32), mine.num_work_tiles, 1)
+    sets = [local.to(device) for _ in range(sets_for(local_bytes(mine)))]
+
+    def call(b) -> None:
+        welm.welmv4_inplace_rope_npu(b.query, b.key, b.positions, b.cache, b.last_index, b.segment_tile_starts)
+
+    us = replay_leg_us([lambda b=b: call(b) for b in sets], dist, device, stream)
+    del sets
+    fresh = local.to(device)
+    call(fresh)
+    check = parity_record(dist, rank, fresh.query, fresh.key, [r[1] - r[0] for r in ranges],
+                          [b.n_tokens for b in batches], MIRROR_CASE)
+    total = sum(local_bytes(b) for b in batches)
+    gbs = total / (us * 1e3)
+    return {
+        "workload": "segmented KV mirror N=16384, BS=128 seeded-uneven requests, split over the GPUs by whole "
+                    "requests (rebased last_index, tile tables rebuilt per GPU)",
+        "scaling": "strong", "requests_per_gpu": [r[1] - r[0] for r in ranges],
+        "tokens_per_gpu": [b.n_tokens for b in batches], "bytes_per_launch": total,
+        "us_per_launch": round(us, 3), "value": round(gbs, 2), "unit": "GB/s",
+        "tokens_per_s": round(16384 / (us * 1e-6), 1), "frac_of_n_gpu_peak": round(gbs / (peak * world), 4),
+        "frac_of_peak_n1_equivalent": round(gbs / peak, 4), "parity": check,
+    }
+
+
+def host_copy_ceiling(h2d: int, d2h: int, steps: int, dist, device, stream) -> dict:
+    """The e2e step's bus traffic as plain copies: h2d bytes from pinned host
+    memory to the device and d2h bytes back, the two directions on two streams
+    at once, on every rank at the same time; max over ranks."""
+    src_h = torch.empty(h2d, dtype=torch.uint8).pin_memory()
+    dst_d = torch.empty(h2d, dtype=torch.uint8, device=device)
+    src_d = torch.empty(d2h, dtype=torch.uint8, device=device)
+    dst_h = torch.empty(d2h, dtype=torch.uint8).pin_memory()
+    side = torch.cuda.Stream(device)
+
+    def step() -> None:
+        side.wait_stream(stream)
+        dst_d.copy_(src_h, non_blocking=True)
+        with torch.cuda.stream(side):
+            dst_h.copy_(src_d, non_blocking=True)
+        stream.wait_stream(side)
+
+    ms = timed_steps(step, steps, dist, device, stream)
+    us = ms * 1e3 / steps
+    return {"us_per_step": round(us, 2), "h2d_gb_s": round(h2d / (us * 1e3), 2), "d2h_gb_s": round(d2h / (us * 1e3), 2),
+            "how": "pinned host -> device and device -> pinned host copies of the e2e step's bytes, both "
+                   "directions at once, every rank at once"}
 
 
 # One configuration of each other benchmark family, timed after the headline
@@ -407,11 +610,27 @@ def run_b200_arm(args) -> int:
     del sets, d_q, d_k, d_p
     torch.cuda.empty_cache()
 
+    peak, peak_kind = hbm_peak()
+    # After timing: the headline's result on pristine inputs, gathered and
+    # checked; then the strong-scaling split of the same request and the
+    # request-sharded segmented KV mirror, each timed and checked the same way;
+    # then the plain host-copy ceiling of the e2e step.  Every rank takes every
+    # step (each holds collectives).
+    fresh = host.to(device)
+    welm.welmv4_inplace_rope_npu(fresh.query, fresh.key, fresh.positions, fresh.cache)
+    headline_parity = parity_record(dist, rank, fresh.query, fresh.key, [TOKENS] * world, [TOKENS] * world,
+                                    PREFILL_CASE, copies=world)
+    del fresh
+    strong = strong_prefill_leg(dist, rank, world, device, stream, peak)
+    mirror = mirror_sharded_leg(dist, rank, world, device, stream, peak)
+    h2d_bytes, d2h_bytes = welm_host.lane_bytes(TOKENS)
+    host_ceiling = host_copy_ceiling(h2d_bytes, d2h_bytes, e2e_steps, dist, device, stream)
+    torch.cuda.empty_cache()
+
     per_step_s = elapsed_ms / 1e3 / args.steps
     total_bytes = algorithmic_bytes(TOKENS) * world
     value = total_bytes / per_step_s / 1e9
     per_launch_gbs = algorithmic_bytes(TOKENS) / per_step_s / 1e9
-    peak, peak_kind = hbm_peak()
     e2e_per_step = e2e_ms / 1e3 / e2e_steps
     full_per_step = full_ms / 1e3 / e2e_steps
     staged_per_step = staged_ms / 1e3 / e2e_steps
@@ -452,6 +671,7 @@ def run_b200_arm(args) -> int:
             "math": "f32 (separate mul/sub/add roundings, one RNE to bf16)",
             "data": "synthetic (seeded N(0,1) bf16 Q/K, positions 0..M-1)",
             "config": workload_config(world),
+            "parity": headline_parity,
             "roofline": {
                 "bound": "hbm",
                 "achieved": round(per_launch_gbs, 2),
@@ -488,6 +708,8 @@ def run_b200_arm(args) -> int:
                 "steps": e2e_steps,
                 "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
+                "host_ceiling": host_ceiling,
+                "frac_of_host_ceiling": round(host_ceiling["us_per_step"] / (e2e_per_step * 1e6), 4),
                 "api": "testfiles_b200.welmv4_inplace_rope_host (pinned host Q/K/positions, mapped transport: "
                        "one kernel reads each 128-byte rope slice from host memory over PCIe and writes it back; "
                        "every transfer in the timed region)",
@@ -507,6 +729,8 @@ def run_b200_arm(args) -> int:
                     "api": "welmv4_inplace_rope_npu on device copies of the whole pinned tensors",
                 },
             },
+            "strong_scaling": strong,
+            "mirror_sharded": mirror,
             "clocks": sampler.summary(),
             "gpu_launches": launches,
             "other_configs": others,
