@@ -130,9 +130,9 @@ int welm_rope_mirror(void* q, void* k, const int64_t* positions,
  * WELM_ROPE_DEV_BAD_LAST_INDEX and is skipped.  batch_size <=
  * WELM_ROPE_LENS_MAX_BATCH (the lengths are staged in shared memory).
  *
- * Row 4 of the path's "next" list (on-device tile building fused with the
- * mirror launch); the reference builds tiles on the host
- * (bench_welmv4_inplace_rope_npu.py:1439-1461) before each launch.
+ * On-device tile building fused with the mirror launch; the reference builds
+ * tiles on the host (bench_welmv4_inplace_rope_npu.py:1439-1461) before each
+ * launch.
  */
 #define WELM_ROPE_LENS_MAX_BATCH 2048
 int welm_rope_mirror_from_lens(void* q, void* k, const int64_t* positions,
@@ -299,10 +299,18 @@ int welm_rope_ordinary_mapped(void* q, void* k, const int64_t* positions,
  * t < n_tokens and writes them back unchanged: the ordinary kernel's accesses
  * without positions, cos/sin and arithmetic (16-byte aligned bases, strides a
  * multiple of 8 elements, else WELM_ROPE_ERR_BAD_STRIDE).
+ * welm_rope_ceiling_gather performs only the ordinary kernel's position and
+ * cos/sin gather for tokens t < n_tokens (the same items, launch shape and
+ * pre-wait hints and prefetches; 16-byte aligned cache, else
+ * WELM_ROPE_ERR_BAD_STRIDE) and writes nothing but, when the values it read
+ * fold to a fixed magic word (they do not for any real cache), one int32 to
+ * `sink`: its L2 and DRAM counters are those of the gather alone.
  */
 int welm_rope_ceiling_copy(void* dst, const void* src, int64_t bytes, void* stream);
 int welm_rope_ceiling_slices(void* q, void* k, int64_t n_tokens, int64_t q_token_stride,
                              int64_t k_token_stride, void* stream);
+int welm_rope_ceiling_gather(const int64_t* positions, const float* cos_sin_cache, int64_t n_tokens,
+                             int64_t max_position, int32_t* sink, void* stream);
 
 /* Human-readable name of a welm_rope_status code (static storage). */
 const char* welm_rope_status_string(int status);
@@ -310,8 +318,9 @@ const char* welm_rope_status_string(int status);
 /* ABI version of this header: (major << 16) | minor.  A minor bump only adds
  * entry points or status codes; a major bump changes an existing signature.
  * 1.1 added welm_rope_ordinary_mapped and WELM_ROPE_ERR_NOT_MAPPED; 1.2 the
- * two measurement kernels welm_rope_ceiling_copy and welm_rope_ceiling_slices. */
-#define WELM_ROPE_ABI_VERSION ((1 << 16) | 2)
+ * two measurement kernels welm_rope_ceiling_copy and welm_rope_ceiling_slices;
+ * 1.3 the measurement kernel welm_rope_ceiling_gather. */
+#define WELM_ROPE_ABI_VERSION ((1 << 16) | 3)
 int welm_rope_abi_version(void);
 
 #ifdef __cplusplus

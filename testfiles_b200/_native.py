@@ -49,6 +49,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "welm_rope_ordinary_mapped": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _P, _P]),
     "welm_rope_ceiling_copy": (ctypes.c_int, [_P, _P, _I64, _P]),
     "welm_rope_ceiling_slices": (ctypes.c_int, [_P, _P, _I64, _I64, _I64, _P]),
+    "welm_rope_ceiling_gather": (ctypes.c_int, [_P, _P, _I64, _I64, _P, _P]),
     "welm_rope_count_tiles_host": (ctypes.c_int, [_P, _I64, _P]),
     "welm_rope_build_tiles_host": (ctypes.c_int, [_P, _I64, _P, _I64, _P, _P]),
     "welm_rope_status_string": (ctypes.c_char_p, [ctypes.c_int]),

@@ -101,6 +101,31 @@ __global__ void __launch_bounds__(kBlock) ceiling_slices_head_kernel(uint16_t* q
   store_back(x, salt);
 }
 
+// The ordinary kernels' gather alone: item (token, part) reads the token's
+// position (a hint before the wait, prefetching the cos/sin lines it names,
+// then the real value) and its part of the cos/sin row, and folds the values
+// it read into one word.
+__global__ void __launch_bounds__(kBlock) ceiling_gather_kernel(const int64_t* positions, const float* cache,
+                                                                int32_t items, int64_t max_position,
+                                                                int32_t* sink) {
+  const int stride = gridDim.x * blockDim.x;
+  const int first = blockIdx.x * blockDim.x + threadIdx.x;
+  if (first < items)
+    prefetch_cos_sin_row(cache, max_position, hint_load(positions + (first >> kPartShift)), first & (kParts - 1));
+  pdl_enter();
+  uint32_t fold = 0;
+  for (int item = first; item < items; item += stride) {
+    const int part = item & (kParts - 1);
+    const int64_t pos = __ldg(positions + (item >> kPartShift));
+    if (pos < 0 || pos >= max_position) continue;
+    CosSin cs;
+    Io<true>::load_cos_sin(cache + pos * kRopeDim, part, cs);
+#pragma unroll
+    for (int i = 0; i < kLanes; ++i) fold ^= __float_as_uint(cs.c[i]) ^ (__float_as_uint(cs.s[i]) << 1);
+  }
+  if (fold == 0x9e3779b9u && sink != nullptr) *sink = int32_t(fold);
+}
+
 }  // namespace
 
 extern "C" {
@@ -146,6 +171,18 @@ int welm_rope_ceiling_slices(void* q, void* k, int64_t n_tokens, int64_t q_token
   return launch(ceiling_slices_kernel, shape.grid, shape.block, 0, st,
                 static_cast<uint16_t*>(q), static_cast<uint16_t*>(k), q_token_stride, k_token_stride,
                 int32_t(items), uint32_t(0));
+}
+
+int welm_rope_ceiling_gather(const int64_t* positions, const float* cos_sin_cache, int64_t n_tokens,
+                             int64_t max_position, int32_t* sink, void* stream) {
+  if (n_tokens < 0 || max_position < 0 || n_tokens > kMaxItems / kParts) return WELM_ROPE_ERR_BAD_SIZE;
+  if (n_tokens == 0) return WELM_ROPE_OK;
+  if (!positions || !cos_sin_cache) return WELM_ROPE_ERR_NULL_POINTER;
+  if (!aligned16(cos_sin_cache)) return WELM_ROPE_ERR_BAD_STRIDE;
+  const int64_t items = n_tokens * kParts;
+  const LaunchShape shape = stream_shape(items);
+  return launch(ceiling_gather_kernel, shape.grid, shape.block, 0, static_cast<cudaStream_t>(stream), positions,
+                cos_sin_cache, int32_t(items), max_position, sink);
 }
 
 }  // extern "C"

@@ -30,6 +30,9 @@ copy kernel, launched like the op (``stream_copy_us``).  Ordinary cases also
 get ``slice_floor_us``: the op's own loads and stores without its gather
 and arithmetic, over the same buffers.
 
+``--gather-only`` (with ``--iters``) launches only the op's position and
+cos/sin gather (``ceiling_gather_kernel``) on the case's positions, so an ncu
+capture of it gives the gather's L2 hit rate apart from the Q/K slices.
 ``--host mapped|staged`` times the host-memory entry instead (ordinary
 cases): Q, K and positions in pinned host memory, every PCIe transfer inside
 the timed region, µs per call and GB/s each way over the bus.
@@ -188,6 +191,24 @@ def ceiling_slices(q: torch.Tensor, k: torch.Tensor) -> None:
     rc = ops._call(q.device, lib.welm_rope_ceiling_slices, q.data_ptr(), k.data_ptr(), int(q.shape[0]),
                    int(q.stride(0)), int(k.stride(0)), torch.cuda.current_stream(q.device).cuda_stream)
     _native.check("welm_rope_ceiling_slices", rc)
+
+
+def ceiling_gather(positions: torch.Tensor, cache: torch.Tensor) -> None:
+    """The ordinary kernels' position and cos/sin gather alone
+    (welm_rope_ceiling_gather) over ``positions``, on the current stream of
+    their device: for profiling the gather's L2 and DRAM traffic apart from
+    the Q/K slices."""
+    if positions.device != cache.device or positions.device.type != "cuda":
+        raise ValueError("ceiling_gather needs positions and cache on one CUDA device")
+    if positions.dtype != torch.int64 or cache.dtype != torch.float32 or cache.dim() != 2 or cache.shape[1] != 64:
+        raise TypeError("ceiling_gather needs int64 positions and a float32 [P, 64] cache")
+    if not (positions.is_contiguous() and cache.is_contiguous()):
+        raise ValueError("ceiling_gather needs contiguous tensors")
+    lib = _native.load()
+    rc = ops._call(positions.device, lib.welm_rope_ceiling_gather, positions.data_ptr(), cache.data_ptr(),
+                   int(positions.numel()), int(cache.shape[0]), None,
+                   torch.cuda.current_stream(positions.device).cuda_stream)
+    _native.check("welm_rope_ceiling_gather", rc)
 
 
 def stream_copy_us(nbytes: int, sets: int, device: torch.device, trials: int = 5, graph_launches: int = 64,
@@ -474,15 +495,19 @@ def kernel_name(case: workloads.Case) -> str:
     return "rope_ordinary_kernel"
 
 
-def launch_case(case: workloads.Case, device: torch.device, iters: int, from_lens: bool = False) -> dict:
+def launch_case(case: workloads.Case, device: torch.device, iters: int, from_lens: bool = False,
+                gather_only: bool = False) -> dict:
     inp = workloads.make_inputs(case, device)
     if from_lens:
         _with_lens(case, inp, device)
     for _ in range(iters):
-        _launch(inp)
+        if gather_only:
+            ceiling_gather(inp.positions, inp.cache)
+        else:
+            _launch(inp)
     torch.cuda.synchronize(device)
     return {"record_type": "launch", **case_fields(case), "iters": iters,
-            "kernel_name": kernel_name(case)}
+            "kernel_name": "ceiling_gather_kernel" if gather_only else kernel_name(case)}
 
 
 def write_csv(records: list[dict], path: str) -> None:
@@ -503,7 +528,7 @@ def write_csv(records: list[dict], path: str) -> None:
 
 def run(cases: Iterable[workloads.Case], device: torch.device, time_it: bool, iters: int,
         out: Optional[str], from_lens: bool = False, copy_ceiling: bool = False,
-        host_transport: Optional[str] = None, shared_cache: bool = False) -> list[dict]:
+        host_transport: Optional[str] = None, shared_cache: bool = False, gather_only: bool = False) -> list[dict]:
     records = []
     sink = open(out, "a") if out else None
     try:
@@ -514,7 +539,7 @@ def run(cases: Iterable[workloads.Case], device: torch.device, time_it: bool, it
                 rec = time_case(case, device, from_lens=from_lens, copy_ceiling=copy_ceiling,
                                 shared_cache=shared_cache)
             else:
-                rec = launch_case(case, device, iters, from_lens)
+                rec = launch_case(case, device, iters, from_lens, gather_only)
             records.append(rec)
             line = json.dumps(rec)
             print(line, flush=True)
@@ -542,6 +567,9 @@ def main(argv: Optional[list[str]] = None) -> int:
                         help="run segmented KV-mirror cases through rope_mirror_from_lens")
     parser.add_argument("--copy-ceiling", action="store_true",
                         help="with --time: also time a same-size device copy (the practical ceiling)")
+    parser.add_argument("--gather-only", action="store_true",
+                        help="with --iters: launch only the position and cos/sin gather (welm_rope_ceiling_gather) "
+                             "on the case's positions, for profiling it apart from the Q/K slices")
     parser.add_argument("--host", choices=("mapped", "staged"), default=None,
                         help="time the host-memory entry on pinned Q/K with this transport (ordinary cases)")
     parser.add_argument("--kv-write", default=None, metavar="N,BS",
@@ -570,7 +598,7 @@ def main(argv: Optional[list[str]] = None) -> int:
                 fh.write(json.dumps(rec) + "\n")
         return 0
     records = run(select_cases(args.cases), device, args.time, args.iters, args.json, args.mirror_from_lens,
-                  args.copy_ceiling, args.host, args.shared_cache)
+                  args.copy_ceiling, args.host, args.shared_cache, args.gather_only)
     if args.csv:
         write_csv(records, args.csv)
     return 0
