@@ -93,7 +93,7 @@ __global__ void __launch_bounds__(kBlock) ceiling_slices_head_kernel(uint16_t* q
   const int64_t tok = slice / kHeadsPerToken;
   const int head = slice - int(tok) * kHeadsPerToken;
   uint16_t* row = head == 0 ? k + tok * k_stride : q + tok * q_stride + (head - 1) * kHeadDim;
-  if (item < items && part == 0) prefetch_row_slices<1>(row, 0);
+  if (item < items && part == 0 && items >= kHeadPrefetchMinItems) prefetch_row_slices<1>(row, 0);
   pdl_enter();
   if (item >= items) return;
   Slices<true, 1> x;

@@ -71,6 +71,13 @@ LaunchShape shape_for(int64_t total) {
 // 1.96 -> 1.70, M=2048 2.30 -> 2.07, M=4096 2.87 -> 2.85 (even).
 constexpr int64_t kHeadSplitMaxTokens = 4096;
 
+// One-head launches prefetch their slice lines before the wait from this many
+// items (1536 tokens) up.  Measured on one B200 (graph replay, L2-cold sets,
+// us per launch, without -> with the prefetch): M=1536 1.89 -> 1.77, M=2048
+// 2.07 -> 1.91, M=4096 2.85 -> 2.56; below that it only adds latency: M=1
+// 0.83 -> 0.90, M=8 0.93 -> 0.99, M=1281 1.89 -> 1.94.
+constexpr int64_t kHeadPrefetchMinItems = int64_t(1536) * kHeadsPerToken * kParts;
+
 // Launch shape of a one-head launch over `tokens` tokens: true when it
 // applies, that is at most kHeadSplitMaxTokens tokens and a grid that gives
 // every (token, head, part) item its own thread.

@@ -130,7 +130,7 @@ __global__ void __launch_bounds__(kBlock, 5) rope_ordinary_stream_kernel(const R
 // heads.  A decode-sized launch then spreads its loads and stores over seven
 // times as many threads and SMs; every thread gathers its part of the cos/sin
 // row itself (L1/L2 hits after the first).  Same arithmetic, same results.
-template <bool kVec>
+template <bool kVec, bool kPrefetch>
 __global__ void __launch_bounds__(kBlock) rope_ordinary_head_kernel(const RopeArgs a) {
   const int item = blockIdx.x * blockDim.x + threadIdx.x;  // the grid covers every item once
   const int part = item & (kParts - 1);
@@ -138,10 +138,10 @@ __global__ void __launch_bounds__(kBlock) rope_ordinary_head_kernel(const RopeAr
   const int64_t tok = slice / kHeadsPerToken;
   const int head = slice - int(tok) * kHeadsPerToken;
   const bool live = item < a.k_items;
-  uint16_t* row = head == 0 ? a.k + tok * a.k_stride : a.q + tok * a.q_stride + (head - 1) * kHeadDim;
   int64_t pos_hint = -1;
-  if (live) {  // before the wait: the head's slice line(s), the position and the cos/sin lines
-    if (kVec && part == 0) prefetch_row_slices<1>(row, 0);
+  if (live) {  // before the wait: the position and the cos/sin lines (and, with kPrefetch, the slice line)
+    if (kPrefetch && kVec && part == 0)
+      prefetch_row_slices<1>(head == 0 ? a.k + tok * a.k_stride : a.q + tok * a.q_stride + (head - 1) * kHeadDim, 0);
     pos_hint = hint_load(a.positions + tok);
     if (head == 0) prefetch_cos_sin_row(a.cache, a.max_position, pos_hint, part);
   }
@@ -149,7 +149,7 @@ __global__ void __launch_bounds__(kBlock) rope_ordinary_head_kernel(const RopeAr
   if (!live) return;
   const int64_t pos = __ldg(a.positions + tok);
   Slices<kVec, 1> x;
-  x.load(row, part);
+  x.load(head == 0 ? a.k + tok * a.k_stride : a.q + tok * a.q_stride + (head - 1) * kHeadDim, part);
   RowGather<kVec> g;
   g.issue(a, -1, pos_hint, part);
   if (!g.finish(a, pos, part)) {
@@ -167,7 +167,8 @@ int launch_ordinary(const Plan& plan, const RopeArgs& a, cudaStream_t s) {
     if (head_split_shape(plan.token_items / kParts, shape)) {
       RopeArgs h = a;
       h.k_items = int32_t(items);
-      return launch(rope_ordinary_head_kernel<kVec>, shape.grid, shape.block, 0, s, h);
+      return items >= kHeadPrefetchMinItems ? launch(rope_ordinary_head_kernel<kVec, true>, shape.grid, shape.block, 0, s, h)
+                                            : launch(rope_ordinary_head_kernel<kVec, false>, shape.grid, shape.block, 0, s, h);
     }
     shape = stream_shape(plan.token_items);
     return launch(rope_ordinary_stream_kernel<kVec>, shape.grid, shape.block, 0, s, a);
