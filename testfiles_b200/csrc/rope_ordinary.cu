@@ -104,23 +104,46 @@ __global__ void __launch_bounds__(kBlock) rope_ordinary_kernel(const RopeArgs a)
 // Launches above one item per thread (more than 4 CTAs per SM) loop, each
 // thread prefetching its next item's lines before it works on the current.
 // ---------------------------------------------------------------------------
-template <bool kVec>
+// Token of a streaming item before the wait, from hint copies of the tile
+// table (slots) or the item itself (dense); -1 when the slot looks empty.
+template <Source kSrc>
+__device__ __forceinline__ int64_t stream_token_hint(const RopeArgs& a, int item) {
+  const int slot = item >> kPartShift;
+  if (kSrc == Source::kDense) return slot;
+  const int tile = slot / kTile, j = slot - tile * kTile;
+  const int64_t b = hint_load_s32(a.tile_starts + tile), e = hint_load_s32(a.tile_starts + tile + 1);
+  return j < e - b && j < kTile && b + j >= 0 && b + j < a.n_tokens ? b + j : -1;
+}
+
+// kDense: item = token * 4 + part.  kTileSlots (segmented tables whose tiles
+// are mostly full): item = slot * 4 + part, 64 slots per tile, slot j of tile
+// i holding token starts[i] + j (slot_token); before the wait the table
+// entries are read as hints to find the token whose lines to prefetch.
+template <bool kVec, Source kSrc>
 __global__ void __launch_bounds__(kBlock, 5) rope_ordinary_stream_kernel(const RopeArgs a) {
+  static_assert(kSrc == Source::kDense || kSrc == Source::kTileSlots, "dense or slot items");
   const int stride = gridDim.x * blockDim.x;
   const int first = blockIdx.x * blockDim.x + threadIdx.x;
-  int64_t hint = -1;
+  int64_t hint = -1, tok_hint = -1;
   if (first < a.k_items) {  // before the wait: the first item's lines
-    prefetch_token<kVec>(a.q, a.k, a.q_stride, a.k_stride, first >> kPartShift, first & (kParts - 1));
-    hint = hint_load(a.positions + (first >> kPartShift));
-    prefetch_cos_sin_row(a.cache, a.max_position, hint, first & (kParts - 1));
+    tok_hint = stream_token_hint<kSrc>(a, first);
+    if (tok_hint >= 0) {
+      prefetch_token<kVec>(a.q, a.k, a.q_stride, a.k_stride, tok_hint, first & (kParts - 1));
+      hint = hint_load(a.positions + tok_hint);
+      prefetch_cos_sin_row(a.cache, a.max_position, hint, first & (kParts - 1));
+    }
   }
   pdl_enter();
   for (int item = first; item < a.k_items; item += stride) {
-    const int next = item + stride;
-    if (next < a.k_items)
-      prefetch_token<kVec>(a.q, a.k, a.q_stride, a.k_stride, next >> kPartShift, next & (kParts - 1));
-    ordinary_token<kVec>(a, item >> kPartShift, item & (kParts - 1), hint);
-    hint = -1;
+    const int part = item & (kParts - 1);
+    if (kSrc == Source::kDense) {
+      const int next = item + stride;
+      if (next < a.k_items) prefetch_token<kVec>(a.q, a.k, a.q_stride, a.k_stride, next >> kPartShift, next & (kParts - 1));
+    }
+    int64_t tok;
+    if (slot_token<kSrc>(a, item >> kPartShift, part, tok))
+      ordinary_token<kVec>(a, tok, part, tok == tok_hint ? hint : -1);
+    hint = tok_hint = -1;
   }
 }
 
@@ -159,6 +182,17 @@ __global__ void __launch_bounds__(kBlock) rope_ordinary_head_kernel(const RopeAr
   x.rotate_store(g.cs);
 }
 
+// Segmented launches run the streaming kernel over tile slots when at least
+// half of the slots can hold a token (2 N >= 64 T), else the token-mapped
+// kernel over the staged table (or its slot source for tables too large to
+// stage), which never launches a thread for an empty slot.  Measured on one
+// B200 (graph replay, L2-cold sets, us per launch, staged table -> slots): the
+// reference's segmented cases M=4096/8 requests 2.87 -> 2.76, M=8192/32 4.18 ->
+// 4.05, M=9616/8 uneven 4.90 -> 4.55, M=16384/8 uneven 6.43 -> 6.15,
+// M=16384/64 6.53 -> 6.29, M=16384/128 uneven (80 % of slots live) 6.68 ->
+// 6.44.
+bool stream_slots(int64_t num_tiles, int64_t n_tokens) { return num_tiles > 0 && 2 * n_tokens >= num_tiles * kTile; }
+
 template <bool kVec>
 int launch_ordinary(const Plan& plan, const RopeArgs& a, cudaStream_t s) {
   if (plan.src == Source::kDense) {
@@ -171,7 +205,16 @@ int launch_ordinary(const Plan& plan, const RopeArgs& a, cudaStream_t s) {
                                             : launch(rope_ordinary_head_kernel<kVec, false>, shape.grid, shape.block, 0, s, h);
     }
     shape = stream_shape(plan.token_items);
-    return launch(rope_ordinary_stream_kernel<kVec>, shape.grid, shape.block, 0, s, a);
+    return launch(rope_ordinary_stream_kernel<kVec, Source::kDense>, shape.grid, shape.block, 0, s, a);
+  }
+  if (stream_slots(a.num_tiles, a.n_tokens)) {
+    RopeArgs h = a;
+    h.k_items = int32_t(int64_t(a.num_tiles) * kTile * kParts);
+    // one item per thread at every size: a slot's token comes from the table,
+    // so a thread looping over slots could not prefetch its next one
+    LaunchShape shape = shape_for(h.k_items);
+    if (shape.block == unsigned(kBlock)) shape.grid = unsigned((int64_t(h.k_items) + kBlock - 1) / kBlock);
+    return launch(rope_ordinary_stream_kernel<kVec, Source::kTileSlots>, shape.grid, shape.block, 0, s, h);
   }
   switch (plan.src) {
     case Source::kTileTable: return launch_plan(rope_ordinary_kernel<kVec, Source::kTileTable>, plan, a, s);

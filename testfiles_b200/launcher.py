@@ -6,8 +6,9 @@
 
 ``--iters N`` launches the op N times eagerly on one buffer set with a fixed
 kernel name per path (``rope_ordinary_head_kernel`` for dense launches of at
-most 4096 tokens, ``rope_ordinary_stream_kernel`` for larger dense launches,
-``rope_ordinary_kernel`` for segmented ones; ``rope_mirror_kernel``), for
+most 4096 tokens, ``rope_ordinary_stream_kernel`` for larger dense launches
+and segmented ones whose tiles are mostly full, ``rope_ordinary_kernel`` for
+other segmented ones; ``rope_mirror_head_kernel``), for
 ``ncu -k regex:…`` captures — the B200 analogue of the reference's msprof
 launch stub (run_welmv4_inplace_rope_prod_m16384_npu.py:1-60).
 
@@ -489,10 +490,13 @@ HEAD_SPLIT_MAX_TOKENS = 4096
 def kernel_name(case: workloads.Case) -> str:
     """The kernel a case's launch runs, for ``ncu -k`` filters."""
     if case.is_mirror:
-        return "rope_mirror_kernel"
+        return "rope_mirror_head_kernel"
     if not case.is_segmented:
         return "rope_ordinary_head_kernel" if case.n_tokens <= HEAD_SPLIT_MAX_TOKENS else "rope_ordinary_stream_kernel"
-    return "rope_ordinary_kernel"
+    # segmented: the streaming kernel over tile slots when at least half of
+    # the slots can hold a token (stream_slots in csrc/rope_ordinary.cu)
+    tiles = len(workloads.tile_starts_for(case.segment_lens)) - 1
+    return "rope_ordinary_stream_kernel" if tiles > 0 and 2 * case.n_tokens >= 64 * tiles else "rope_ordinary_kernel"
 
 
 def launch_case(case: workloads.Case, device: torch.device, iters: int, from_lens: bool = False,

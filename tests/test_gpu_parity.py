@@ -386,6 +386,27 @@ def test_device_built_tables_drive_the_mirror_kernel():
     assert_bitexact(dev.key, k_ref, "key")
 
 
+@pytest.mark.parametrize("lens", [
+    (1,) * 128 + (3968,),            # 190 tiles for 4096 tokens: staged-table kernel (under half the slots live)
+    (64,) * 64,                      # every slot live: streaming kernel over tile slots
+    tuple(workloads.seeded_uneven_lens(20000, 300, 3)),  # about 80 % of slots live, more than one wave of slots
+    (5, 70, 1, 130, 64, 63, 65) * 9,  # partial tiles of every length, just over half the slots live
+])
+def test_segmented_prefill_routes_match_oracle(lens):
+    """Segmented ordinary prefill takes the streaming kernel over tile slots
+    when at least half of the slots can hold a token, else the kernel over the
+    staged table; both must equal the oracle."""
+    n = sum(lens)
+    case = workloads.Case("adhoc_routes", "segmented_prefill", n, 0, lens, flavour="baseline")
+    inp = workloads.make_inputs(case, "cpu")
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    dev = run_drop_in(inp, status)
+    q_ref, k_ref = rope_oracle.reference_outputs(inp.query, inp.key, inp.positions, inp.last_index, inp.cache)
+    assert_bitexact(dev.query, q_ref, "query")
+    assert_bitexact(dev.key, k_ref, "key")
+    assert status.item() == 0
+
+
 @pytest.mark.parametrize("mirror", [False, True])
 def test_large_tile_tables_match_oracle(mirror):
     """Thousands of short requests: more tiles than the shared-memory table

@@ -314,5 +314,7 @@ def test_launcher_kernel_names_follow_the_head_split_rule():
     assert launcher.kernel_name(workloads.find_case("b_decode_m1")) == "rope_ordinary_head_kernel"
     assert launcher.kernel_name(workloads.find_case("b_prefill_m4096")) == "rope_ordinary_head_kernel"
     assert launcher.kernel_name(workloads.find_case("b_prefill_m4097")) == "rope_ordinary_stream_kernel"
-    assert launcher.kernel_name(workloads.find_case("segmented_m4096_b8_aligned")) == "rope_ordinary_kernel"
-    assert launcher.kernel_name(workloads.find_case("b_mirror_contiguous_n8192")) == "rope_mirror_kernel"
+    assert launcher.kernel_name(workloads.find_case("segmented_m4096_b8_aligned")) == "rope_ordinary_stream_kernel"
+    sparse = workloads.Case("sparse", "segmented_prefill", 4096, 129, (1,) * 128 + (3968,))
+    assert launcher.kernel_name(sparse) == "rope_ordinary_kernel"  # 190 tiles, 4096 tokens: under half the slots
+    assert launcher.kernel_name(workloads.find_case("b_mirror_contiguous_n8192")) == "rope_mirror_head_kernel"
