@@ -10,22 +10,6 @@ namespace {
 // (bench_welmv4_inplace_rope_npu.py:856-919).  Q rows and K rows are disjoint
 // tensors, so the two phases need no ordering.
 //
-// Finishes a six-head Q row whose gather g was issued (with or without hints)
-// before src was known.
-template <bool kVec>
-__device__ __forceinline__ void finish_q_row(const RopeArgs& a, Slices<kVec, kQHeads>& qx, int64_t src,
-                                             RowGather<kVec>& g, int part) {
-  if (src < 0 || src >= a.n_tokens) {
-    if (part == 0) raise_status(a.status, WELM_ROPE_DEV_BAD_LAST_INDEX);
-    return;
-  }
-  if (!g.finish(a, g.position(a, src), part)) {
-    if (part == 0) raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
-    return;
-  }
-  qx.rotate_store(g.cs);
-}
-
 // ---------------------------------------------------------------------------
 // KV-mirror prefill, one head per item.  Items [0, q_items) are Q heads, item
 // = (row * 6 + head) * 4 + part.  The K items follow: with has_segments = 0
@@ -128,7 +112,11 @@ __global__ void __launch_bounds__(kBlock, 8) rope_mirror_head_kernel(const RopeA
 // the dependency wait, warps holding Q rows run the same scan over hint
 // copies of the lengths so each row's source position and cos/sin row can be
 // loaded speculatively; the real scan keeps them only if the hints held.  One
-// item per thread: Q rows, then K tokens.
+// item per thread, one head per item: Q heads, then K tokens.  Measured on one
+// B200 (graph replay, L2-cold sets, us per launch) against the previous
+// six-head-row kernel without data prefetch: N=16384 BS=128 uneven 3.71 ->
+// 3.34, N=16384 BS=32 3.21 -> 2.70, N=9616 BS=8 2.83 -> 2.36, N=8192 BS=2
+// 2.68 -> 2.27.  A preferred shared-memory carveout of 50 % was slower.
 // ---------------------------------------------------------------------------
 constexpr int kLensCap = WELM_ROPE_LENS_MAX_BATCH;
 
@@ -166,53 +154,60 @@ __device__ __forceinline__ int64_t warp_request_ends(Load load, int n, int row, 
   return total;
 }
 
-// At most 128 registers, so 4 CTAs fit per SM and a 16384-token launch
-// (516 CTAs) stays resident in one wave on 148 SMs.
+// The same from request lengths, one head per item: items [0, q_items) are
+// Q heads (row * 6 + head) * 4 + part, then K tokens token * 4 + part.  Before
+// the wait, warps holding Q items run the length scan on hint copies of the
+// lengths to find each row's source token and warm its position and cos/sin
+// lines; every item prefetches its slice line.  After the wait the lengths
+// are staged in shared memory (cp.async) while the data loads fly, and after
+// the one barrier each warp derives the total and its rows' ends with
+// shuffles; the Q heads keep their speculative loads only if the hints held.
 template <bool kVec>
-__global__ void __launch_bounds__(kBlock, 4) rope_mirror_lens_kernel(const RopeArgs a, const int64_t* lens, int batch) {
+__global__ void __launch_bounds__(kBlock, 8) rope_mirror_lens_head_kernel(const RopeArgs a, const int64_t* lens,
+                                                                          int batch) {
   extern __shared__ int64_t s_len[];
-  // Before the wait: K tokens warm their cos/sin row; warps holding Q rows
-  // scan hint copies of the lengths for each row's source token and warm
-  // that token's row (the real scan after the barrier confirms the hints).
-  int64_t src_hint = -1, pos_hint = -1;
-  prefetch_lines(lens, int64_t(batch) * sizeof(int64_t));
-  {
-    const int item0 = blockIdx.x * blockDim.x + threadIdx.x;
-    if ((item0 & ~31) < a.q_items) {  // warp-uniform: the scan shuffles
-      int64_t end_hint = 0;
-      bool neg_hint = false;
-      warp_request_ends([&](int i) { return hint_load(lens + i); }, batch,
-                        item0 < a.q_items ? (item0 >> kPartShift) : -1, end_hint, neg_hint);
-      if (item0 < a.q_items) {
-        src_hint = end_hint - 1;
-        if (src_hint >= 0 && src_hint < a.n_tokens) pos_hint = hint_load(a.positions + src_hint);
-      }
-    }
-    if (item0 >= a.q_items && item0 - a.q_items < a.k_items)
-      pos_hint = hint_load(a.positions + ((item0 - a.q_items) >> kPartShift));
-    prefetch_cos_sin_row(a.cache, a.max_position, pos_hint, item0 & (kParts - 1));
-  }
-  pdl_enter();
-  for (int j = threadIdx.x; j < batch; j += blockDim.x) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(s_len + j)), "l"(lens + j) : "memory");
-  }
-  asm volatile("cp.async.commit_group;" ::: "memory");
   const int item = blockIdx.x * blockDim.x + threadIdx.x;
   const int part = item & (kParts - 1);
   const bool is_q = item < a.q_items;
   const int k_item = item - a.q_items;
-  const bool is_token = !is_q && k_item < a.k_items;
-  const int64_t tok = is_token ? (k_item >> kPartShift) : 0;
-  Slices<kVec, kQHeads> qx;
-  Slices<kVec, 1> kx;
+  const bool is_k = !is_q && k_item < a.k_items;
+  const int64_t tok = is_k ? (k_item >> kPartShift) : 0;
+  const int q_slice = is_q ? (item >> kPartShift) : 0;
+  const int row = q_slice / kQHeads;
+  const int head = q_slice - row * kQHeads;
+  uint16_t* slice_row = is_q ? a.q + int64_t(row) * a.q_stride + head * kHeadDim : a.k + tok * a.k_stride;
+
+  // Before the wait: hints and prefetches only.
+  prefetch_lines(lens, int64_t(batch) * sizeof(int64_t));
+  int64_t src_hint = -1, pos_hint = -1;
+  if ((item & ~31) < a.q_items) {  // warp-uniform: the scan shuffles
+    int64_t end_hint = 0;
+    bool neg_hint = false;
+    warp_request_ends([&](int i) { return hint_load(lens + i); }, batch, is_q ? row : -1, end_hint, neg_hint);
+    if (is_q) {
+      src_hint = end_hint - 1;
+      if (src_hint >= 0 && src_hint < a.n_tokens) pos_hint = hint_load(a.positions + src_hint);
+    }
+  }
+  if (is_q || is_k) {
+    if (kVec && part == 0) prefetch_row_slices<1>(slice_row, 0);
+    if (is_k) pos_hint = hint_load(a.positions + tok);
+  }
+  prefetch_cos_sin_row(a.cache, a.max_position, pos_hint, part);
+  pdl_enter();
+
+  for (int j = threadIdx.x; j < batch; j += blockDim.x)
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(s_len + j)), "l"(lens + j) : "memory");
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  Slices<kVec, 1> x;
   RowGather<kVec> g;
   bool pos_ok = false;
   if (is_q) {
-    qx.load(a.q + int64_t(item >> kPartShift) * a.q_stride, part);
+    x.load(slice_row, part);
     g.issue(a, src_hint, pos_hint, part);
-  } else if (is_token) {
+  } else if (is_k) {
     const int64_t pos = __ldg(a.positions + tok);
-    kx.load(a.k + tok * a.k_stride, part);
+    x.load(slice_row, part);
     g.issue(a, -1, pos_hint, part);
     pos_ok = g.finish(a, pos, part);
   }
@@ -220,13 +215,20 @@ __global__ void __launch_bounds__(kBlock, 4) rope_mirror_lens_kernel(const RopeA
   __syncthreads();
   int64_t end_row = 0;
   bool negative = false;
-  const int64_t total = warp_request_ends([&](int i) { return s_len[i]; }, batch,
-                                          is_q ? (item >> kPartShift) : -1, end_row, negative);
+  const int64_t total = warp_request_ends([&](int i) { return s_len[i]; }, batch, is_q ? row : -1, end_row, negative);
   if (is_q) {
-    finish_q_row<kVec>(a, qx, end_row - 1, g, part);  // keeps the speculative loads only if the hints held
-  } else if (is_token && tok < total) {
+    const bool flag = part == 0 && head == 0;  // one report per row
+    const int64_t src = end_row - 1;
+    if (src < 0 || src >= a.n_tokens) {
+      if (flag) raise_status(a.status, WELM_ROPE_DEV_BAD_LAST_INDEX);
+    } else if (!g.finish(a, g.position(a, src), part)) {
+      if (flag) raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
+    } else {
+      x.rotate_store(g.cs);
+    }
+  } else if (is_k && tok < total) {
     if (pos_ok) {
-      kx.rotate_store(g.cs);
+      x.rotate_store(g.cs);
     } else if (part == 0) {
       raise_status(a.status, WELM_ROPE_DEV_BAD_POSITION);
     }
@@ -234,9 +236,6 @@ __global__ void __launch_bounds__(kBlock, 4) rope_mirror_lens_kernel(const RopeA
   if (negative && blockIdx.x == 0 && threadIdx.x == 0) raise_status(a.status, WELM_ROPE_DEV_BAD_LENGTH);
 }
 
-// Launch of the one-head kernel: one item per thread, in warp-sized CTAs while
-// the launch is below one 128-thread CTA per SM (its items then spread over
-// every SM), else in 128-thread CTAs.
 template <typename Kernel>
 int launch_heads(Kernel kernel, int64_t total, const RopeArgs& a, cudaStream_t s) {
   const int sms = current_sm_count();
@@ -309,7 +308,8 @@ int welm_rope_mirror_from_lens(void* q, void* k, const int64_t* positions, const
                                int64_t q_token_stride, int64_t k_token_stride, int64_t max_position,
                                int32_t* device_status, void* stream) {
   if (n_tokens < 0 || batch_size < 0 || max_position < 0) return WELM_ROPE_ERR_BAD_SIZE;
-  if (batch_size > kLensCap || n_tokens > kMaxItems / kParts - kLensCap) return WELM_ROPE_ERR_BAD_SIZE;
+  if (batch_size > kLensCap || n_tokens > (kMaxItems - int64_t(kLensCap) * kQHeads * kParts) / kParts)
+    return WELM_ROPE_ERR_BAD_SIZE;
   if (batch_size == 0 || n_tokens == 0) return WELM_ROPE_OK;  // no request, or no token to rotate
   if (!q || !k || !positions || !cos_sin_cache || !seq_lens) return WELM_ROPE_ERR_NULL_POINTER;
   if ((batch_size > 1 && q_token_stride < kQHeads * kHeadDim) || (n_tokens > 1 && k_token_stride < kHeadDim))
@@ -325,17 +325,19 @@ int welm_rope_mirror_from_lens(void* q, void* k, const int64_t* positions, const
   a.n_tokens = n_tokens;
   a.max_position = max_position;
   a.status = device_status;
-  a.q_items = int32_t(batch_size * kParts);
+  a.q_items = int32_t(batch_size * kQHeads * kParts);
   a.k_items = int32_t(n_tokens * kParts);
   const bool vec = aligned16(q) && aligned16(k) && aligned16(cos_sin_cache) &&
                    (batch_size <= 1 || q_token_stride % 8 == 0) && (n_tokens <= 1 || k_token_stride % 8 == 0);
   const int64_t total = int64_t(a.q_items) + a.k_items;
-  const unsigned grid = unsigned((total + kBlock - 1) / kBlock);
   const size_t smem = size_t(batch_size) * sizeof(int64_t);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int b = int(batch_size);
-  return vec ? launch(rope_mirror_lens_kernel<true>, grid, kBlock, smem, s, a, seq_lens, b)
-             : launch(rope_mirror_lens_kernel<false>, grid, kBlock, smem, s, a, seq_lens, b);
+  const int sms = current_sm_count();
+  const unsigned block = sms > 0 && total <= int64_t(sms) * kBlock ? 32u : unsigned(kBlock);
+  const unsigned grid = unsigned((total + block - 1) / block);
+  return vec ? launch(rope_mirror_lens_head_kernel<true>, grid, block, smem, s, a, seq_lens, b)
+             : launch(rope_mirror_lens_head_kernel<false>, grid, block, smem, s, a, seq_lens, b);
 }
 
 }  // extern "C"
