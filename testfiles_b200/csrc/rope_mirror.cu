@@ -64,6 +64,11 @@ __global__ void __launch_bounds__(kBlock, 8) rope_mirror_head_kernel(const RopeA
       pos_hint = hint_load(a.positions + tok_hint);
     }
   }
+  // Unlike the ordinary streaming kernel, the mirror keeps its cos/sin
+  // prefetch before the wait even though it waits on the hint: every CTA of
+  // the next launch is resident about 1.5 us early, and without it the
+  // contiguous mirror (16384 distinct rows from DRAM) slowed from 2.26 to
+  // 2.75 us.
   prefetch_cos_sin_row(a.cache, a.max_position, pos_hint, part);
   pdl_enter();
 

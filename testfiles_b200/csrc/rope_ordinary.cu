@@ -128,9 +128,13 @@ __global__ void __launch_bounds__(kBlock, 5) rope_ordinary_stream_kernel(const R
   if (first < a.k_items) {  // before the wait: the first item's lines
     tok_hint = stream_token_hint<kSrc>(a, first);
     if (tok_hint >= 0) {
+      // The position is read as a hint but not waited for: the cos/sin loads
+      // at the hinted position start right after the wait (ordinary_token's
+      // RowGather).  Prefetching the cos/sin lines here would stall the
+      // thread on the hint before it reaches the wait; CTAs that start late
+      // then release late (M=16384: 5.80 us without that prefetch, 6.15 with).
       prefetch_token<kVec>(a.q, a.k, a.q_stride, a.k_stride, tok_hint, first & (kParts - 1));
       hint = hint_load(a.positions + tok_hint);
-      prefetch_cos_sin_row(a.cache, a.max_position, hint, first & (kParts - 1));
     }
   }
   pdl_enter();
@@ -212,7 +216,7 @@ int launch_ordinary(const Plan& plan, const RopeArgs& a, cudaStream_t s) {
     h.k_items = int32_t(int64_t(a.num_tiles) * kTile * kParts);
     // one item per thread at every size: a slot's token comes from the table,
     // so a thread looping over slots could not prefetch its next one
-    LaunchShape shape = shape_for(h.k_items);
+    LaunchShape shape = stream_shape(h.k_items);
     if (shape.block == unsigned(kBlock)) shape.grid = unsigned((int64_t(h.k_items) + kBlock - 1) / kBlock);
     return launch(rope_ordinary_stream_kernel<kVec, Source::kTileSlots>, shape.grid, shape.block, 0, s, h);
   }
