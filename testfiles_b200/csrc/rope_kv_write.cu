@@ -63,7 +63,7 @@ __global__ void __launch_bounds__(kBlock) rope_mirror_kv_write_kernel(const KvAr
   // row's head through the last_index hint; K: the K and V rows, and the
   // slot-mapping line).  Like every pre-wait access these only warm L2.
   // Measured on one B200 (graph replay, L2-cold sets, us per launch):
-  // N=16384 BS=128 7.34 -> 6.44, N=8192 BS=8 4.56 -> 4.19, N=BS=128 unchanged.
+  // N=16384 BS=128 7.34 -> 6.38, N=8192 BS=8 4.56 -> 3.94, N=BS=128 unchanged.
   {
     const int part0 = item0 & (kParts - 1);
     if (item0 < a.q_items) {
@@ -78,8 +78,10 @@ __global__ void __launch_bounds__(kBlock) rope_mirror_kv_write_kernel(const KvAr
       if (a.v != nullptr) prefetch_line(a.v + tok * a.v_stride + part0 * 64);
       if (part0 == 1 && (reinterpret_cast<uintptr_t>(a.slots + tok) & 127u) < sizeof(int64_t))
         prefetch_line(a.slots + tok);
+      // the position hint feeds the speculative cos/sin loads after the wait;
+      // it is not waited for here (prefetching its cos/sin lines before the
+      // wait stalled late CTAs: N=8192 BS=8 4.18 us with it, 3.94 without)
       pos_hint = hint_load(a.positions + tok);
-      prefetch_cos_sin_row(a.cache, a.max_position, pos_hint, part0);
     }
   }
   pdl_enter();
