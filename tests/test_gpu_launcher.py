@@ -90,3 +90,20 @@ def test_ceiling_kernels_copy_exactly_and_leave_slices_unchanged():
         torch.cuda.synchronize()
         assert torch.equal(q.view(torch.int16), q0.view(torch.int16)), rows
         assert torch.equal(k.view(torch.int16), k0.view(torch.int16)), rows
+
+
+def test_gather_ceiling_reads_without_writing():
+    """welm_rope_ceiling_gather runs the op's position and cos/sin gather alone:
+    it returns without error on every launch shape, rejects bad tensors on the
+    host, and writes nothing (its sink is never set for a real cache)."""
+    cache = workloads.make_cos_sin_cache(16384, 10000.0, device=DEV)
+    for m in (1, 100, 5000, 16384, 40000):  # warp-sized CTAs, 128-thread CTAs, and looping threads
+        pos = (torch.arange(m, device=DEV, dtype=torch.int64) * 7) % 16384
+        pos_before, cache_before = pos.clone(), cache.clone()
+        launcher.ceiling_gather(pos, cache)
+        torch.cuda.synchronize()
+        assert torch.equal(pos, pos_before) and torch.equal(cache, cache_before), m
+    with pytest.raises(TypeError):
+        launcher.ceiling_gather(pos.to(torch.int32), cache)
+    with pytest.raises(ValueError):
+        launcher.ceiling_gather(pos[::2], cache)

@@ -303,6 +303,12 @@ def test_ceiling_entries_host_validation():
     assert slices(FAKE, FAKE, 4, 1535, 256, None) == _native.ERR_BAD_STRIDE
     assert slices(FAKE, FAKE, 4, 1540, 256, None) == _native.ERR_BAD_STRIDE  # not 8-aligned
     assert slices(FAKE, FAKE + 2, 4, 1536, 256, None) == _native.ERR_BAD_STRIDE
+    gather = lib.welm_rope_ceiling_gather
+    assert gather(FAKE, FAKE, -1, 64, None, None) == _native.ERR_BAD_SIZE
+    assert gather(FAKE, FAKE, 4, -1, None, None) == _native.ERR_BAD_SIZE
+    assert gather(None, None, 0, 64, None, None) == _native.OK
+    assert gather(None, FAKE, 4, 64, None, None) == _native.ERR_NULL_POINTER
+    assert gather(FAKE, FAKE + 8, 4, 64, None, None) == _native.ERR_BAD_STRIDE  # the cache is read in 16-byte vectors
 
 
 def test_launcher_kernel_names_follow_the_head_split_rule():
