@@ -14,15 +14,20 @@
 // exactly as the reference's separate torch elementwise ops round.
 //
 // Work decomposition (B200-first, not the reference's 56-program tile loop):
-//   * one work item = (row, part): a thread owns 8 lanes of x1 and the
-//     matching 8 lanes of x2 of every head of that row, i.e. two 16-byte
-//     vectors per head; 4 threads cover a row's 128-byte rope slice per head;
-//   * the thread loads its 8 cos + 8 sin values once (four 16-byte loads) and
-//     reuses them from registers for all heads of the row (7 for the ordinary
-//     op: 1 K + 6 Q), so each cache row crosses HBM once per token;
-//   * every data load of the row is issued before the position-dependent
-//     cache load, so the position -> cache dependency overlaps the data
-//     stream; the grid is sized so a whole prefill is resident in one wave.
+//   * a thread owns 8 lanes of x1 and the matching 8 lanes of x2 of a head,
+//     i.e. two 16-byte vectors; 4 threads ("parts") cover a head's 128-byte
+//     rope slice.  A work item is (row, part) with seven heads (the ordinary
+//     streaming and segmented kernels: each cos/sin row then crosses HBM once
+//     per token and is reused from registers for 1 K + 6 Q heads), or
+//     (row, head, part) with one head (small ordinary launches and the KV
+//     mirror, so more threads share a launch and fewer registers are held);
+//   * the thread loads its 8 cos + 8 sin values once (four 16-byte loads);
+//   * launches use programmatic dependent launch: before the dependency wait
+//     a thread only reads hints and prefetches lines into L2, which cannot
+//     change a result, and after it every data load of the item is issued
+//     before the position-dependent cache load (or next to a speculative one
+//     at the hinted position), so the position -> cache dependency overlaps
+//     the data stream;
 //   * 64-token work tiles are kept only as the segment / masking unit of the
 //     reference's contract; positions are gathered per token, so no
 //     contiguity inside a tile is assumed (bench_welmv4_inplace_rope_npu.py:714-715
@@ -93,12 +98,14 @@ __device__ __forceinline__ void pdl_enter() {
 }
 
 // Work done BEFORE pdl_enter(), while the previous grid may still run: a
-// thread reads its position as a hint only (ld.global.cg: served from L2,
-// never allocated in L1, so no stale L1 line can answer the real loads made
-// after the wait) and prefetches that cos/sin row into L2.  A prefetch cannot
-// change a result — L2 is where writes of the previous grid land — and a
-// stale or garbage hint only fetches a useless line; hints outside the cache
-// are ignored.  The results use the positions read after the wait.
+// thread reads its position (and table entries or last_index) as hints only
+// (ld.global.cg: served from L2, never allocated in L1, so no stale L1 line
+// can answer the real loads made after the wait), and prefetches into L2 the
+// lines its item will read: its rope slices and, in some kernels, the cos/sin
+// row at the hinted position.  A prefetch cannot change a result — L2 is where
+// writes of the previous grid land — and a stale or garbage hint only fetches
+// a useless line; hints outside the cache are ignored.  The results use the
+// values read after the wait.
 __device__ __forceinline__ int64_t hint_load(const int64_t* p) {
   int64_t v;
   asm volatile("ld.global.cg.s64 %0, [%1];" : "=l"(v) : "l"(p));
