@@ -46,3 +46,45 @@ def test_result_line_configuration():
     assert cfg["global_tokens"] == 4 * bench.TOKENS and cfg["parallelism"] == "request-sharded dp4"
     assert bench.BUFFER_SETS * bench.algorithmic_bytes(bench.TOKENS) > 2 * 126 * 1024 * 1024
     assert set(bench.OTHER_CONFIGS) <= {c.name for c in workloads.baseline_cases()}
+
+
+def test_sharded_outputs_concatenate_to_the_golden_digests():
+    """The bench checks multi-GPU legs by gathering each rank's rows and
+    comparing their SHA-256 with the unsharded golden digest.  That only works
+    if the shards' outputs, concatenated in rank order, are the unsharded
+    outputs: checked here with the oracle on the CPU for the request-sharded
+    segmented mirror and the token-sharded prefill at 1, 2, 3 and 8 ranks."""
+    import torch
+
+    from oracle import rope_oracle
+    from testfiles_b200 import sharding
+
+    bench = load_bench()
+    case = workloads.find_case(bench.MIRROR_CASE)
+    full = workloads.make_inputs(case, "cpu")
+    want = bench.golden_outputs(bench.MIRROR_CASE)
+    for world in (1, 2, 3, 8):
+        qs, ks = [], []
+        for rr in sharding.shard_requests(case.segment_lens, world):
+            b = sharding.local_batch(case.segment_lens, rr, full.last_index.tolist())
+            t0, t1 = b.token_begin, b.token_end
+            q, k = rope_oracle.tiled_outputs(full.query[rr[0]:rr[1]], full.key[t0:t1], full.positions[t0:t1],
+                                             full.cache, b.num_work_tiles, 1, b.tile_starts,
+                                             torch.tensor(b.last_index))
+            qs.append(q)
+            ks.append(k)
+        assert bench.sha256_rows(torch.cat(qs)) == want["query"], world
+        assert bench.sha256_rows(torch.cat(ks)) == want["key"], world
+    case = workloads.find_case(bench.PREFILL_CASE)
+    full = workloads.make_inputs(case, "cpu")
+    want = bench.golden_outputs(bench.PREFILL_CASE)
+    for world in (2, 8):
+        qs, ks = [], []
+        for r in range(world):
+            t0, t1 = sharding.shard_tokens(bench.TOKENS, world, r)
+            q, k = rope_oracle.reference_outputs(full.query[t0:t1], full.key[t0:t1], full.positions[t0:t1], None,
+                                                 full.cache)
+            qs.append(q)
+            ks.append(k)
+        assert bench.sha256_rows(torch.cat(qs)) == want["query"], world
+        assert bench.sha256_rows(torch.cat(ks)) == want["key"], world
