@@ -12,7 +12,7 @@
 //   8.7 MB it took 2.80 against 3.26.
 // * welm_rope_ceiling_slices: the ordinary dense kernels' own access pattern —
 //   the same item mapping (seven heads per thread, or one head per thread for
-//   launches of at most 4096 tokens), launch shape, pre-wait prefetch of the
+//   launches of at most 3328 tokens), launch shape, pre-wait prefetch of the
 //   slice lines, and 16-byte loads and stores of the rope slices of K and the
 //   six Q heads, in place — without the position and cos/sin gather and
 //   without the arithmetic.  Its time is the floor of that access pattern:

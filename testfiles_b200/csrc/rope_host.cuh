@@ -64,12 +64,13 @@ LaunchShape shape_for(int64_t total) {
 }
 
 // Dense launches of at most this many tokens run one head per thread (the
-// ordinary one-head kernel, and the slice ceiling that mirrors it).  Measured
-// on one B200 (graph replay, L2-cold sets, us per launch, seven heads per
-// thread -> one): M=1 1.12 -> 0.86, M=8 1.22 -> 0.94, M=32 1.35 -> 1.09,
-// M=128 1.47 -> 1.15, M=256 1.49 -> 1.18, M=577 1.61 -> 1.35, M=1024
-// 1.96 -> 1.70, M=2048 2.30 -> 2.07, M=4096 2.87 -> 2.85 (even).
-constexpr int64_t kHeadSplitMaxTokens = 4096;
+// ordinary one-head kernel, and the slice ceiling that mirrors it); larger
+// ones run the streaming kernel.  Measured on one B200 (graph replay, L2-cold
+// sets, us per launch): against a seven-heads-per-thread launch without
+// prefetch, M=1 1.12 -> 0.86, M=128 1.47 -> 1.15, M=1024 1.96 -> 1.70; one
+// head per thread against the streaming kernel, M=2048 1.91 vs 2.23, M=2561
+// 2.08 vs 2.23, M=3072 2.29 vs 2.36, M=3585 2.54 vs 2.50, M=4096 2.70 vs 2.59.
+constexpr int64_t kHeadSplitMaxTokens = 3328;
 
 // One-head launches prefetch their slice lines before the wait from this many
 // items (1536 tokens) up.  Measured on one B200 (graph replay, L2-cold sets,

@@ -6,7 +6,7 @@
 
 ``--iters N`` launches the op N times eagerly on one buffer set with a fixed
 kernel name per path (``rope_ordinary_head_kernel`` for dense launches of at
-most 4096 tokens, ``rope_ordinary_stream_kernel`` for larger dense launches
+most 3328 tokens, ``rope_ordinary_stream_kernel`` for larger dense launches
 and segmented ones whose tiles are mostly full, ``rope_ordinary_kernel`` for
 other segmented ones; ``rope_mirror_head_kernel``), for
 ``ncu -k regex:…`` captures — the B200 analogue of the reference's msprof
@@ -484,7 +484,7 @@ def time_fused_qkv(n_tokens: int, device: torch.device, trials: int = 7, graph_l
 
 # Dense ordinary launches of at most this many tokens run one head per thread
 # (kHeadSplitMaxTokens in csrc/rope_host.cuh).
-HEAD_SPLIT_MAX_TOKENS = 4096
+HEAD_SPLIT_MAX_TOKENS = 3328
 
 
 def kernel_name(case: workloads.Case) -> str:

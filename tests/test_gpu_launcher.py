@@ -82,7 +82,7 @@ def test_ceiling_kernels_copy_exactly_and_leave_slices_unchanged():
     launcher.ceiling_slices(qkv[:, :1536].view(m, 6, 256), qkv[:, 1536:1792].view(m, 1, 256))
     torch.cuda.synchronize()
     assert torch.equal(qkv.view(torch.int16), before.view(torch.int16))
-    for rows in (3001, 5000):  # one head per thread up to 4096 tokens, seven above
+    for rows in (3001, 5000):  # one head per thread up to 3328 tokens, seven above
         q = torch.randn((rows, 6, 256), device=DEV, generator=g).to(torch.bfloat16)
         k = torch.randn((rows, 1, 256), device=DEV, generator=g).to(torch.bfloat16)
         q0, k0 = q.clone(), k.clone()

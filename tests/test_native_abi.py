@@ -318,8 +318,8 @@ def test_launcher_kernel_names_follow_the_head_split_rule():
     limit = int(re.search(r"constexpr int64_t kHeadSplitMaxTokens = (\d+);", src).group(1))
     assert launcher.HEAD_SPLIT_MAX_TOKENS == limit
     assert launcher.kernel_name(workloads.find_case("b_decode_m1")) == "rope_ordinary_head_kernel"
-    assert launcher.kernel_name(workloads.find_case("b_prefill_m4096")) == "rope_ordinary_head_kernel"
-    assert launcher.kernel_name(workloads.find_case("b_prefill_m4097")) == "rope_ordinary_stream_kernel"
+    assert launcher.kernel_name(workloads.find_case("b_prefill_m3328")) == "rope_ordinary_head_kernel"
+    assert launcher.kernel_name(workloads.find_case("b_prefill_m3329")) == "rope_ordinary_stream_kernel"
     assert launcher.kernel_name(workloads.find_case("segmented_m4096_b8_aligned")) == "rope_ordinary_stream_kernel"
     sparse = workloads.Case("sparse", "segmented_prefill", 4096, 129, (1,) * 128 + (3968,))
     assert launcher.kernel_name(sparse) == "rope_ordinary_kernel"  # 190 tiles, 4096 tokens: under half the slots
