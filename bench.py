@@ -121,6 +121,16 @@ def max_over_ranks(dist, value: float, device) -> float:
     return float(t.item())
 
 
+def all_ranks(dist, value: float, device) -> list[float]:
+    """Every rank's value, in rank order (after the timed region)."""
+    if dist is None:
+        return [value]
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    out = [torch.zeros_like(t) for _ in range(dist.get_world_size())]
+    dist.all_gather(out, t)
+    return [float(x.item()) for x in out]
+
+
 def barrier(dist, device) -> None:
     if dist is not None:
         dist.barrier(device_ids=[device.index])
@@ -580,7 +590,9 @@ def run_b200_arm(args) -> int:
         end.record(stream)
         barrier(dist, device)
         launches += args.steps
-        elapsed_ms = max_over_ranks(dist, start.elapsed_time(end), device)
+        own_ms = start.elapsed_time(end)
+        elapsed_ms = max_over_ranks(dist, own_ms, device)
+        rank_ms = all_ranks(dist, own_ms, device)
 
         # End to end through the public host-memory API: Q, K and positions
         # start in pinned host memory every step and the rotated Q and K end
@@ -693,6 +705,7 @@ def run_b200_arm(args) -> int:
             "warmup": args.warmup,
             "ms_per_step": round(per_step_s * 1e3, 6),
             "us_per_launch": round(per_step_s * 1e6, 3),
+            "rank_us_per_launch": [round(ms * 1e3 / args.steps, 3) for ms in rank_ms],
             "tokens_per_s": round(TOKENS * world / per_step_s, 1),
             "higher_is_better": True,
             "scaling": "weak",
