@@ -594,6 +594,15 @@ def run_b200_arm(args) -> int:
         elapsed_ms = max_over_ranks(dist, own_ms, device)
         rank_ms = all_ranks(dist, own_ms, device)
 
+    # One configuration of each other family (one GPU only), timed right
+    # after the headline and before the host-memory legs: in one process,
+    # later device launches measured up to 20 % slower after the staged host
+    # transport had run (M=8192 3.50 -> 4.19 us, not every time), so every
+    # device-side record is taken before it.  `clocks` covers the headline
+    # only; the legs after it get their own sampler (`clocks_legs`).
+    others = other_config_records(device) if world == 1 and not args.no_config_sweep else None
+
+    with ClockSampler(device.index) as legs_sampler:
         # End to end through the public host-memory API: Q, K and positions
         # start in pinned host memory every step and the rotated Q and K end
         # there (only the rotated lanes cross PCIe).
@@ -683,7 +692,6 @@ def run_b200_arm(args) -> int:
     line = None
     if rank == 0:
         cpu = None
-        others = other_config_records(device) if world == 1 and not args.no_config_sweep else None
         if world == 1:
             times, threads = cpu_reference_time(host, runs=5)
             cpu_t = statistics.median(times)
@@ -777,6 +785,7 @@ def run_b200_arm(args) -> int:
             "strong_scaling": strong,
             "mirror_sharded": mirror,
             "clocks": sampler.summary(),
+            "clocks_legs": legs_sampler.summary(),
             "gpu_launches": launches,
             "other_configs": others,
             "gpu_launches_e2e": launches_e2e,
