@@ -594,15 +594,53 @@ def run_b200_arm(args) -> int:
         elapsed_ms = max_over_ranks(dist, own_ms, device)
         rank_ms = all_ranks(dist, own_ms, device)
 
-    # One configuration of each other family (one GPU only), timed right
-    # after the headline and before the host-memory legs: in one process,
-    # later device launches measured up to 20 % slower after the staged host
-    # transport had run (M=8192 3.50 -> 4.19 us, not every time), so every
-    # device-side record is taken before it.  `clocks` covers the headline
-    # only; the legs after it get their own sampler (`clocks_legs`).
-    others = other_config_records(device) if world == 1 and not args.no_config_sweep else None
-
+    # Every device-only leg runs before the host-memory legs: in one process,
+    # device launches timed after the staged host transport had run measured
+    # up to 20 % slower (prefill M=8192 3.50 -> 4.19 us; the strong-scaled
+    # M=8192 half 3.5 -> 4.3), so the e2e legs come last.  `clocks` covers the
+    # headline only; everything after it gets its own sampler (`clocks_legs`).
+    del body, tail
     with ClockSampler(device.index) as legs_sampler:
+        # One configuration of each other family (one GPU only).
+        others = other_config_records(device) if world == 1 and not args.no_config_sweep else None
+
+        # Same-size copy ceiling: a plain device copy moving the same number of
+        # bytes per step (half read, half written), replayed and timed exactly
+        # like the op, over rotating buffers larger than L2.
+        half = algorithmic_bytes(TOKENS) // 2 // 4096 * 4096  # 4 KiB multiple: the copy's fast path
+        pairs = [(torch.empty(half, dtype=torch.uint8, device=device).fill_(1),
+                  torch.empty(half, dtype=torch.uint8, device=device)) for _ in range(BUFFER_SETS)]
+        copy_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(copy_graph):
+            for i in range(GRAPH_LAUNCHES):
+                src, dst = pairs[i % BUFFER_SETS]
+                dst.copy_(src)
+        copy_ms = timed_steps(copy_graph.replay, 20, dist, device, stream) / (20 * GRAPH_LAUNCHES)
+        del copy_graph, pairs
+        # Two tighter ceilings, each rank on its own (no collective): the same
+        # bytes through the library's streaming copy kernel launched like the
+        # op, and the op's own loads and stores over its buffers without the
+        # position / cos-sin gather and the arithmetic.
+        stream_copy_us = launcher.stream_copy_us(algorithmic_bytes(TOKENS), BUFFER_SETS, device, graph_launches=64)
+        slice_floor_us = launcher.slice_floor_us([(q, k) for q, k, _, _ in sets], device, graph_launches=64)
+        torch.cuda.synchronize(device)
+        del sets
+        torch.cuda.empty_cache()
+
+        peak, peak_kind = hbm_peak()
+        # The headline's result on pristine inputs, gathered and checked; then
+        # the strong-scaling split of the same request and the request-sharded
+        # segmented KV mirror, each timed and checked the same way.  Every rank
+        # takes every step (each holds collectives).
+        fresh = host.to(device)
+        welm.welmv4_inplace_rope_npu(fresh.query, fresh.key, fresh.positions, fresh.cache)
+        headline_parity = parity_record(dist, rank, fresh.query, fresh.key, [TOKENS] * world, [TOKENS] * world,
+                                        PREFILL_CASE, copies=world)
+        del fresh
+        strong = strong_prefill_leg(dist, rank, world, device, stream, peak)
+        mirror = mirror_sharded_leg(dist, rank, world, device, stream, peak)
+        torch.cuda.empty_cache()
+
         # End to end through the public host-memory API: Q, K and positions
         # start in pinned host memory every step and the rotated Q and K end
         # there (only the rotated lanes cross PCIe).
@@ -624,7 +662,8 @@ def run_b200_arm(args) -> int:
 
         # The same through whole-tensor copies (what a caller without the
         # host API would do), reported beside it.
-        d_q, d_k, d_p = torch.empty_like(sets[0][0]), torch.empty_like(sets[0][1]), torch.empty_like(positions)
+        d_q, d_k, d_p = torch.empty_like(h_q, device=device), torch.empty_like(h_k, device=device), \
+            torch.empty_like(positions)
 
         def full_copy_step() -> None:
             d_q.copy_(h_q, non_blocking=True)
@@ -635,48 +674,11 @@ def run_b200_arm(args) -> int:
             h_k.copy_(d_k, non_blocking=True)
 
         full_ms = timed_steps(full_copy_step, e2e_steps, dist, device, stream)
-
-        # Same-size copy ceiling: a plain device copy moving the same number of
-        # bytes per step (half read, half written), replayed and timed exactly
-        # like the op, over rotating buffers larger than L2.
-        half = algorithmic_bytes(TOKENS) // 2 // 4096 * 4096  # 4 KiB multiple: the copy's fast path
-        pairs = [(torch.empty(half, dtype=torch.uint8, device=device).fill_(1),
-                  torch.empty(half, dtype=torch.uint8, device=device)) for _ in range(BUFFER_SETS)]
-        copy_graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(copy_graph):
-            for i in range(GRAPH_LAUNCHES):
-                src, dst = pairs[i % BUFFER_SETS]
-                dst.copy_(src)
-        copy_ms = timed_steps(copy_graph.replay, 20, dist, device, stream) / (20 * GRAPH_LAUNCHES)
-        del copy_graph, pairs
-        # Two tighter ceilings, each rank on its own (no collective): the same
-        # bytes through the library's streaming copy kernel launched like the
-        # op, and the op's own loads and stores over its buffers without the
-        # position / cos-sin gather and the arithmetic.
-        stream_copy_us = launcher.stream_copy_us(algorithmic_bytes(TOKENS), BUFFER_SETS, device, graph_launches=64)
-        slice_floor_us = launcher.slice_floor_us([(q, k) for q, k, _, _ in sets], device, graph_launches=64)
+        del d_q, d_k, d_p
+        # the plain host-copy ceilings of the e2e step
+        h2d_bytes, d2h_bytes = welm_host.lane_bytes(TOKENS)
+        host_ceiling = host_copy_ceiling(h2d_bytes, d2h_bytes, e2e_steps, dist, device, stream, h_q, h_k, h_p)
     torch.cuda.synchronize(device)
-    del body, tail
-    # the timed legs are done: release their device buffers before the
-    # configuration sweep allocates its own
-    del sets, d_q, d_k, d_p
-    torch.cuda.empty_cache()
-
-    peak, peak_kind = hbm_peak()
-    # After timing: the headline's result on pristine inputs, gathered and
-    # checked; then the strong-scaling split of the same request and the
-    # request-sharded segmented KV mirror, each timed and checked the same way;
-    # then the plain host-copy ceiling of the e2e step.  Every rank takes every
-    # step (each holds collectives).
-    fresh = host.to(device)
-    welm.welmv4_inplace_rope_npu(fresh.query, fresh.key, fresh.positions, fresh.cache)
-    headline_parity = parity_record(dist, rank, fresh.query, fresh.key, [TOKENS] * world, [TOKENS] * world,
-                                    PREFILL_CASE, copies=world)
-    del fresh
-    strong = strong_prefill_leg(dist, rank, world, device, stream, peak)
-    mirror = mirror_sharded_leg(dist, rank, world, device, stream, peak)
-    h2d_bytes, d2h_bytes = welm_host.lane_bytes(TOKENS)
-    host_ceiling = host_copy_ceiling(h2d_bytes, d2h_bytes, e2e_steps, dist, device, stream, h_q, h_k, h_p)
     torch.cuda.empty_cache()
 
     per_step_s = elapsed_ms / 1e3 / args.steps
