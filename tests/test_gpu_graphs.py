@@ -130,3 +130,59 @@ def test_segmented_mirror_replays_with_moving_request_boundaries(cache, entry):
         q_ref, k_ref = rope_oracle.reference_outputs(hq, hk, hp, last, host_cache)
         assert torch.equal(bits(q), q_ref.view(torch.int16)), lens
         assert torch.equal(bits(k), k_ref.view(torch.int16)), lens
+
+
+# Ordinary segmented prefill with the device builder in the graph: the table
+# changes from replay to replay (same tile count), so tile-slot items whose
+# pre-wait table hints name another token must reload.  The lengths sum to
+# fewer than N tokens, so the tail stays unrotated.  "slots": most slots
+# live (streaming kernel over tile slots); "table": 40 short requests, so
+# most slots are empty (token-mapped kernel over the staged table).
+ORDINARY_LENS_SETS = {
+    "slots": ([100, 200, 250], [250, 200, 100], [150, 150, 250]),
+    "table": tuple([(7 * i + s) % 10 + 1 for i in range(40)] for s in (0, 3, 6)),
+}
+
+
+@pytest.mark.parametrize("kind", sorted(ORDINARY_LENS_SETS))
+def test_segmented_prefill_replays_with_moving_request_boundaries(cache, kind):
+    host_cache, dev_cache = cache
+    sets = ORDINARY_LENS_SETS[kind]
+    n, bs = 600, len(sets[0])
+    tiles = {welm.count_segment_tiles(lens) for lens in sets}
+    assert len(tiles) == 1
+    tiles = tiles.pop()
+    assert all(sum(lens) <= n for lens in sets)
+    lens_src = torch.empty(bs, dtype=torch.int64, device=DEV)
+    q_src = torch.empty((n, 6, 256), dtype=torch.bfloat16, device=DEV)
+    k_src = torch.empty((n, 1, 256), dtype=torch.bfloat16, device=DEV)
+    p_src = torch.empty(n, dtype=torch.int64, device=DEV)
+    lens_dev, q, k, p = (torch.empty_like(t) for t in (lens_src, q_src, k_src, p_src))
+    capacity = -(-n // 64) + bs + 1
+
+    def load(lens, seed):
+        pos = within_request_positions(lens)
+        pos = torch.cat([pos, torch.zeros(n - pos.numel(), dtype=torch.int64)])
+        host = (torch.tensor(lens, dtype=torch.int64), seeded((n, 6, 256), seed), seeded((n, 1, 256), seed + 1), pos)
+        for s, h in zip((lens_src, q_src, k_src, p_src), host):
+            s.copy_(h)
+        return host
+
+    def step():
+        lens_dev.copy_(lens_src)
+        q.copy_(q_src)
+        k.copy_(k_src)
+        p.copy_(p_src)
+        starts, _, _ = welm.build_segment_tile_starts_device(lens_dev, capacity)
+        welm.rope_prefill(q, k, p, dev_cache, starts, tiles, n, q.stride(0), k.stride(0), 1)
+
+    load(sets[0], 1)
+    graph = capture(step)
+    for i, lens in enumerate(sets * 2):
+        _, hq, hk, hp = load(lens, 40 + i)
+        graph.replay()
+        torch.cuda.synchronize()
+        table = rope_oracle.build_tile_starts(lens)
+        q_ref, k_ref = rope_oracle.tiled_outputs(hq, hk, hp, host_cache, tiles, 1, table)
+        assert torch.equal(bits(q), q_ref.view(torch.int16)), lens
+        assert torch.equal(bits(k), k_ref.view(torch.int16)), lens
