@@ -79,13 +79,24 @@ constexpr int64_t kHeadSplitMaxTokens = 3328;
 // 0.83 -> 0.90, M=8 0.93 -> 0.99, M=1281 1.89 -> 1.94.
 constexpr int64_t kHeadPrefetchMinItems = int64_t(1536) * kHeadsPerToken * kParts;
 
+// One-head launches of at most this many 128-thread CTAs' worth of items
+// (decode batches up to 22 tokens) run in 128-thread CTAs rather than the
+// warp-sized CTAs of shape_for.  Measured on four B200 boxes (graph replay,
+// us per launch, warp-sized -> 128-thread CTAs): M=8 0.93 -> 0.90 and 1.00
+// -> 0.99, M=12 1.05 -> 0.99, M=16 1.08 -> 0.90 / 0.92 / 0.99, M=20 1.07 ->
+// 1.02.  From seven CTAs up it depends on the box: M=32 1.09 -> 0.93 on two
+// boxes but 1.09 -> 1.18 on the other two, so larger batches keep the warp-
+// sized CTAs.  256-thread CTAs were slower still (M=40 1.18, M=128 1.47).
+constexpr int64_t kHeadFewCtas = 5;
+
 // Launch shape of a one-head launch over `tokens` tokens: true when it
 // applies, that is at most kHeadSplitMaxTokens tokens and a grid that gives
 // every (token, head, part) item its own thread.
 bool head_split_shape(int64_t tokens, LaunchShape& shape) {
   if (tokens > kHeadSplitMaxTokens) return false;
   const int64_t items = tokens * kHeadsPerToken * kParts;
-  shape = shape_for(items);
+  shape = items <= kHeadFewCtas * kBlock ? LaunchShape{unsigned((items + kBlock - 1) / kBlock), unsigned(kBlock)}
+                                         : shape_for(items);
   return int64_t(shape.grid) * shape.block >= items;
 }
 

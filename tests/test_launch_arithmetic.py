@@ -20,6 +20,7 @@ PARTS = 4
 HEADS = 7  # the K head and six Q heads
 SRC = (REPO / "testfiles_b200" / "csrc" / "rope_host.cuh").read_text()
 HEAD_SPLIT_MAX = int(re.search(r"constexpr int64_t kHeadSplitMaxTokens = (\d+);", SRC).group(1))
+HEAD_FEW_CTAS = int(re.search(r"constexpr int64_t kHeadFewCtas = (\d+);", SRC).group(1))
 
 
 def grid_for(items: int) -> int:
@@ -37,11 +38,14 @@ def head_split_shape(tokens: int):
     if tokens > HEAD_SPLIT_MAX:
         return None
     items = tokens * HEADS * PARTS
-    grid, block = shape_for(items)
+    if items <= HEAD_FEW_CTAS * BLOCK:
+        grid, block = (items + BLOCK - 1) // BLOCK, BLOCK
+    else:
+        grid, block = shape_for(items)
     return (grid, block) if grid * block >= items else None
 
 
-@pytest.mark.parametrize("tokens", [1, 2, 3, 17, 127, 128, 338, 1353, 1354, 2048, 3327, 3328])
+@pytest.mark.parametrize("tokens", [1, 2, 3, 17, 22, 23, 127, 128, 338, 1353, 1354, 2048, 3327, 3328])
 def test_one_head_items_cover_every_slice_once(tokens):
     grid, block = head_split_shape(tokens)
     item = np.arange(grid * block)
@@ -59,6 +63,8 @@ def test_one_head_items_cover_every_slice_once(tokens):
 def test_one_head_rule_applies_up_to_the_limit_only():
     assert all(head_split_shape(t) is not None for t in range(1, HEAD_SPLIT_MAX + 1))
     assert head_split_shape(HEAD_SPLIT_MAX + 1) is None
+    # decode batches up to 22 tokens run in at most kHeadFewCtas 128-thread CTAs
+    assert head_split_shape(22) == (5, BLOCK) and head_split_shape(23)[1] == 32
 
 
 @pytest.mark.parametrize("vectors", [1, 127, 303104, 303105, 524288, 1212416, 1310723, 2_100_000])
@@ -92,6 +98,7 @@ def test_restated_rules_match_the_sources():
     assert "const int64_t cap = sms > 0 ? int64_t(sms) * 16 : need;" in SRC  # grid_for
     assert "if (sms > 0 && total <= int64_t(sms) * kBlock)" in SRC  # warp-sized table CTAs
     assert "const int64_t items = tokens * kHeadsPerToken * kParts;" in SRC  # head_split_shape
+    assert "shape = items <= kHeadFewCtas * kBlock ? LaunchShape{unsigned((items + kBlock - 1) / kBlock)" in SRC
     assert "const int64_t wave = int64_t(sms > 0 ? sms : 1) * 16 * kBlock;" in ceiling
     assert "const int64_t need = (vectors + 4 * kBlock - 1) / (4 * kBlock);" in ceiling
 
