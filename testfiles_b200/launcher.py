@@ -249,15 +249,19 @@ def slice_floor_us(buffers: list[tuple[torch.Tensor, torch.Tensor]], device: tor
 
 def time_case(case: workloads.Case, device: torch.device, trials: int = 5, graph_launches: int = 64,
               replays: Optional[int] = None, from_lens: bool = False, copy_ceiling: bool = False,
-              shared_cache: bool = False) -> dict:
+              shared_cache: bool = False, sets: Optional[int] = None) -> dict:
     """µs per launch of ``case`` (graph-replayed over rotating buffer sets);
     ``from_lens`` runs segmented mirror cases through rope_mirror_from_lens.
     ``shared_cache`` gives every set the same cos/sin cache (hot in L2, as
-    in serving) instead of a private copy each."""
+    in serving) instead of a private copy each.  ``sets`` overrides the
+    number of buffer sets (default: enough that more than twice the L2
+    lies between reuses, at most 64); one or two keep the data L2-resident."""
     host = workloads.make_inputs(case, "cpu")
     nbytes = workloads.min_bytes(case)
-    sets_needed = max(2, -(-2 * L2_BYTES // max(nbytes, 1)))
-    sets = int(min(64, sets_needed))
+    if sets is None:
+        sets = int(min(64, max(2, -(-2 * L2_BYTES // max(nbytes, 1)))))
+    elif sets < 1:
+        raise ValueError("sets must be at least 1")
     buffers = []
     base = host.to(device)
     for _ in range(sets):
@@ -532,7 +536,8 @@ def write_csv(records: list[dict], path: str) -> None:
 
 def run(cases: Iterable[workloads.Case], device: torch.device, time_it: bool, iters: int,
         out: Optional[str], from_lens: bool = False, copy_ceiling: bool = False,
-        host_transport: Optional[str] = None, shared_cache: bool = False, gather_only: bool = False) -> list[dict]:
+        host_transport: Optional[str] = None, shared_cache: bool = False, gather_only: bool = False,
+        sets: Optional[int] = None) -> list[dict]:
     records = []
     sink = open(out, "a") if out else None
     try:
@@ -541,7 +546,7 @@ def run(cases: Iterable[workloads.Case], device: torch.device, time_it: bool, it
                 rec = time_host_case(case, device, host_transport)
             elif time_it:
                 rec = time_case(case, device, from_lens=from_lens, copy_ceiling=copy_ceiling,
-                                shared_cache=shared_cache)
+                                shared_cache=shared_cache, sets=sets)
             else:
                 rec = launch_case(case, device, iters, from_lens, gather_only)
             records.append(rec)
@@ -567,6 +572,9 @@ def main(argv: Optional[list[str]] = None) -> int:
     parser.add_argument("--csv", default=None, help="write all records as one CSV table here")
     parser.add_argument("--shared-cache", action="store_true",
                         help="with --time: one cos/sin cache for all buffer sets (hot in L2, as in serving)")
+    parser.add_argument("--sets", type=int, default=None,
+                        help="with --time: rotate this many buffer sets (the copy ceilings too) instead of "
+                             "enough to keep L2 cold; 1 or 2 keep every byte L2-resident")
     parser.add_argument("--mirror-from-lens", action="store_true",
                         help="run segmented KV-mirror cases through rope_mirror_from_lens")
     parser.add_argument("--copy-ceiling", action="store_true",
@@ -583,6 +591,8 @@ def main(argv: Optional[list[str]] = None) -> int:
                         help="time prefill on strided Q/K views of an [M, 8 x 256] QKV output against a "
                              "contiguous Q copy followed by the op")
     args = parser.parse_args(argv)
+    if args.sets is not None and args.sets < 1:
+        parser.error("--sets needs at least 1")
     if not torch.cuda.is_available():
         print("the launcher needs a CUDA device", file=sys.stderr)
         return 2
@@ -602,7 +612,7 @@ def main(argv: Optional[list[str]] = None) -> int:
                 fh.write(json.dumps(rec) + "\n")
         return 0
     records = run(select_cases(args.cases), device, args.time, args.iters, args.json, args.mirror_from_lens,
-                  args.copy_ceiling, args.host, args.shared_cache, args.gather_only)
+                  args.copy_ceiling, args.host, args.shared_cache, args.gather_only, args.sets)
     if args.csv:
         write_csv(records, args.csv)
     return 0

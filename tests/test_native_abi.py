@@ -311,6 +311,17 @@ def test_ceiling_entries_host_validation():
     assert gather(FAKE, FAKE + 8, 4, 64, None, None) == _native.ERR_BAD_STRIDE  # the cache is read in 16-byte vectors
 
 
+def test_launcher_rejects_fewer_than_one_buffer_set():
+    import torch
+
+    from testfiles_b200 import launcher, workloads
+
+    with pytest.raises(SystemExit):
+        launcher.main(["--time", "--sets", "0"])
+    with pytest.raises(ValueError, match="sets"):
+        launcher.time_case(workloads.find_case("b_decode_m1"), torch.device("cpu"), sets=0)
+
+
 def test_launcher_kernel_names_follow_the_head_split_rule():
     from testfiles_b200 import launcher, workloads
 
