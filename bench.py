@@ -319,9 +319,11 @@ def parity_record(dist, rank: int, q: torch.Tensor, k: torch.Tensor, q_counts: l
     }
 
 
-def replay_leg_us(launches: list, dist, device, stream, graph_launches: int = 64, replays: int = 8) -> float:
+def replay_leg_us(launches: list, dist, device, stream, graph_launches: int = 64,
+                  replays: int = 8) -> tuple[float, list[float]]:
     """Max-over-ranks µs per launch of `launches` (one callable per buffer
-    set, used in rotation), replayed from a warmed CUDA graph."""
+    set, used in rotation), replayed from a warmed CUDA graph, and every
+    rank's own µs per launch in rank order."""
     for f in launches[:3]:
         f()
     torch.cuda.synchronize(device)
@@ -340,9 +342,12 @@ def replay_leg_us(launches: list, dist, device, stream, graph_launches: int = 64
         g.replay()
     end.record(stream)
     barrier(dist, device)
-    ms = max_over_ranks(dist, start.elapsed_time(end), device)
+    own = start.elapsed_time(end)
+    ms = max_over_ranks(dist, own, device)
+    ranks = all_ranks(dist, own, device)
     del g
-    return ms * 1e3 / (replays * graph_launches)
+    per = 1e3 / (replays * graph_launches)
+    return ms * per, [round(x * per, 3) for x in ranks]
 
 
 def sets_for(nbytes: int) -> int:
@@ -363,8 +368,8 @@ def strong_prefill_leg(dist, rank: int, world: int, device, stream, peak: float)
     t0, t1 = ranges[rank]
     local = workloads.Inputs(host.query[t0:t1], host.key[t0:t1], host.positions[t0:t1], host.cache)
     sets = [local.to(device) for _ in range(sets_for(algorithmic_bytes(t1 - t0)))]
-    us = replay_leg_us([lambda b=b: welm.welmv4_inplace_rope_npu(b.query, b.key, b.positions, b.cache)
-                        for b in sets], dist, device, stream)
+    us, rank_us = replay_leg_us([lambda b=b: welm.welmv4_inplace_rope_npu(b.query, b.key, b.positions, b.cache)
+                                 for b in sets], dist, device, stream)
     del sets
     fresh = local.to(device)
     welm.welmv4_inplace_rope_npu(fresh.query, fresh.key, fresh.positions, fresh.cache)
@@ -373,7 +378,7 @@ def strong_prefill_leg(dist, rank: int, world: int, device, stream, peak: float)
     gbs = algorithmic_bytes(TOKENS) / (us * 1e3)
     return {
         "workload": "ordinary prefill M=16384 (one request) split over the GPUs in 64-aligned token ranges",
-        "scaling": "strong", "tokens_per_gpu": counts, "us_per_launch": round(us, 3),
+        "scaling": "strong", "tokens_per_gpu": counts, "us_per_launch": round(us, 3), "rank_us_per_launch": rank_us,
         "value": round(gbs, 2), "unit": "GB/s", "tokens_per_s": round(TOKENS / (us * 1e-6), 1),
         "frac_of_n_gpu_peak": round(gbs / (peak * world), 4), "parity": check,
     }
@@ -408,7 +413,7 @@ def mirror_sharded_leg(dist, rank: int, world: int, device, stream, peak: float)
     def call(b) -> None:
         welm.welmv4_inplace_rope_npu(b.query, b.key, b.positions, b.cache, b.last_index, b.segment_tile_starts)
 
-    us = replay_leg_us([lambda b=b: call(b) for b in sets], dist, device, stream)
+    us, rank_us = replay_leg_us([lambda b=b: call(b) for b in sets], dist, device, stream)
     del sets
     fresh = local.to(device)
     call(fresh)
@@ -421,7 +426,7 @@ def mirror_sharded_leg(dist, rank: int, world: int, device, stream, peak: float)
                     "requests (rebased last_index, tile tables rebuilt per GPU)",
         "scaling": "strong", "requests_per_gpu": [r[1] - r[0] for r in ranges],
         "tokens_per_gpu": [b.n_tokens for b in batches], "bytes_per_launch": total,
-        "us_per_launch": round(us, 3), "value": round(gbs, 2), "unit": "GB/s",
+        "us_per_launch": round(us, 3), "rank_us_per_launch": rank_us, "value": round(gbs, 2), "unit": "GB/s",
         "tokens_per_s": round(16384 / (us * 1e-6), 1), "frac_of_n_gpu_peak": round(gbs / (peak * world), 4),
         "frac_of_peak_n1_equivalent": round(gbs / peak, 4), "parity": check,
     }
