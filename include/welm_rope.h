@@ -62,6 +62,7 @@ typedef enum welm_rope_status {
 #define WELM_ROPE_DEV_BAD_TILE 4       /* tile start/end outside [0, N], or > 64 tokens */
 #define WELM_ROPE_DEV_BAD_LENGTH 8     /* negative request length (tile builder)        */
 #define WELM_ROPE_DEV_BAD_SLOT 16      /* slot_mapping[t] >= num_slots (KV-cache write) */
+#define WELM_ROPE_DEV_WAIT_TIMEOUT 32  /* a bounded barrier wait gave up (TMA ceiling)   */
 
 /* Fixed model contract (bench_welmv4_inplace_rope_npu.py:48-58): head_dim 256, rope_dim 64, 6 Q heads,
  * 1 K head, 64-token work tiles. */
@@ -305,12 +306,28 @@ int welm_rope_ordinary_mapped(void* q, void* k, const int64_t* positions,
  * WELM_ROPE_ERR_BAD_STRIDE) and writes nothing but, when the values it read
  * fold to a fixed magic word (they do not for any real cache), one int32 to
  * `sink`: its L2 and DRAM counters are those of the gather alone.
+ *
+ * welm_rope_ceiling_tma_slices moves the same slices as
+ * welm_rope_ceiling_slices through shared memory with the Tensor Memory
+ * Accelerator: `ctas` persistent CTAs (0: two per SM), each with a ring of
+ * `stages` (2, 4 or 6; else WELM_ROPE_ERR_BAD_MODE) 16-token tiles loaded by
+ * tiled cp.async.bulk.tensor and stored back unchanged by bulk-tensor stores,
+ * the first tiles prefetched into L2 before the dependency wait.  Strides of
+ * at least one row (1536 and 256 elements) and multiples of 8 elements,
+ * 16-byte aligned bases (else WELM_ROPE_ERR_BAD_STRIDE); n_tokens at most
+ * 2^31 - 17 (else WELM_ROPE_ERR_BAD_SIZE); WELM_ROPE_ERR_CUDA when the driver
+ * cannot encode the tensor maps.  A barrier wait that gives up ORs
+ * WELM_ROPE_DEV_WAIT_TIMEOUT into device_status (when non-NULL) and ends
+ * that CTA's work.
  */
 int welm_rope_ceiling_copy(void* dst, const void* src, int64_t bytes, void* stream);
 int welm_rope_ceiling_slices(void* q, void* k, int64_t n_tokens, int64_t q_token_stride,
                              int64_t k_token_stride, void* stream);
 int welm_rope_ceiling_gather(const int64_t* positions, const float* cos_sin_cache, int64_t n_tokens,
                              int64_t max_position, int32_t* sink, void* stream);
+int welm_rope_ceiling_tma_slices(void* q, void* k, int64_t n_tokens, int64_t q_token_stride,
+                                 int64_t k_token_stride, int32_t ctas, int32_t stages, int32_t* device_status,
+                                 void* stream);
 
 /* Human-readable name of a welm_rope_status code (static storage). */
 const char* welm_rope_status_string(int status);
@@ -319,8 +336,9 @@ const char* welm_rope_status_string(int status);
  * entry points or status codes; a major bump changes an existing signature.
  * 1.1 added welm_rope_ordinary_mapped and WELM_ROPE_ERR_NOT_MAPPED; 1.2 the
  * two measurement kernels welm_rope_ceiling_copy and welm_rope_ceiling_slices;
- * 1.3 the measurement kernel welm_rope_ceiling_gather. */
-#define WELM_ROPE_ABI_VERSION ((1 << 16) | 3)
+ * 1.3 the measurement kernel welm_rope_ceiling_gather; 1.4 the measurement
+ * kernel welm_rope_ceiling_tma_slices and WELM_ROPE_DEV_WAIT_TIMEOUT. */
+#define WELM_ROPE_ABI_VERSION ((1 << 16) | 4)
 int welm_rope_abi_version(void);
 
 #ifdef __cplusplus

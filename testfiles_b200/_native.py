@@ -32,6 +32,7 @@ DEV_BAD_LAST_INDEX = 2
 DEV_BAD_TILE = 4
 DEV_BAD_LENGTH = 8
 DEV_BAD_SLOT = 16
+DEV_WAIT_TIMEOUT = 32
 
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
@@ -50,6 +51,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "welm_rope_ceiling_copy": (ctypes.c_int, [_P, _P, _I64, _P]),
     "welm_rope_ceiling_slices": (ctypes.c_int, [_P, _P, _I64, _I64, _I64, _P]),
     "welm_rope_ceiling_gather": (ctypes.c_int, [_P, _P, _I64, _I64, _P, _P]),
+    "welm_rope_ceiling_tma_slices": (ctypes.c_int, [_P, _P, _I64, _I64, _I64, ctypes.c_int32, ctypes.c_int32, _P,
+                                                    _P]),
     "welm_rope_count_tiles_host": (ctypes.c_int, [_P, _I64, _P]),
     "welm_rope_build_tiles_host": (ctypes.c_int, [_P, _I64, _P, _I64, _P, _P]),
     "welm_rope_status_string": (ctypes.c_char_p, [ctypes.c_int]),

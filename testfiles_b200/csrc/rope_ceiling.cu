@@ -17,6 +17,14 @@
 //   six Q heads, in place — without the position and cos/sin gather and
 //   without the arithmetic.  Its time is the floor of that access pattern:
 //   what the op would take if the rotation were free.
+// * welm_rope_ceiling_tma_slices: the same slices moved through shared memory
+//   by the Tensor Memory Accelerator instead of the threads' own loads and
+//   stores — persistent CTAs, each with a ring of 16-token tiles loaded by
+//   tiled cp.async.bulk.tensor and stored back unchanged by bulk-tensor
+//   stores — so the register path can be compared with TMA staging on the
+//   op's own buffers.
+
+#include <cudaTypedefs.h>
 
 #include "rope_host.cuh"
 
@@ -126,6 +134,166 @@ __global__ void __launch_bounds__(kBlock) ceiling_gather_kernel(const int64_t* p
   if (fold == 0x9e3779b9u && sink != nullptr) *sink = int32_t(fold);
 }
 
+// ---------------------------------------------------------------------------
+// TMA-staged slice mover.  Tile i holds tokens [16 i, 16 i + 16): the rope
+// lanes (x = 192..255) of Q's six heads as one 3-D box {64 lanes, 6 heads, 16
+// tokens} (12 KB) and of K as one 2-D box {64 lanes, 16 tokens} (2 KB).  CTA
+// b takes tiles b, b + G, b + 2G, ... through a ring of S stages: one elected
+// thread arms the stage's mbarrier with the 14 KB it expects, issues both
+// loads, waits for them, issues both stores from the same shared memory and,
+// once the stores have read it, refills the stage with the tile S steps
+// ahead.  Loads past the last token fill zeros and stores past it are
+// clipped, so ragged N needs no special case.  Before the dependency wait the
+// CTA's first S tiles are prefetched into L2 (a prefetch returns no data, so
+// it cannot see stale values).  Every barrier wait gives up after a bounded
+// number of polls, raises WELM_ROPE_DEV_WAIT_TIMEOUT and ends the CTA's work.
+// ---------------------------------------------------------------------------
+constexpr int kTmaTileTokens = 16;
+constexpr int kTmaQBytes = kRopeDim * 2 * kQHeads * kTmaTileTokens;
+constexpr int kTmaKBytes = kRopeDim * 2 * kTmaTileTokens;
+constexpr int kTmaStageBytes = kTmaQBytes + kTmaKBytes;
+constexpr int kTmaWaitPolls = 1 << 22;
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arm(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_poll(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+__device__ __forceinline__ void tma_tile_load(uint8_t* stage, const CUtensorMap* qmap, const CUtensorMap* kmap,
+                                              int tile, uint64_t* bar) {
+  const int z = tile * kTmaTileTokens;
+  mbar_arm(bar, kTmaStageBytes);
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+      ::"r"(smem_u32(stage)), "l"(qmap), "r"(kRopeLane0), "r"(0), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_u32(stage + kTmaQBytes)), "l"(kmap), "r"(kRopeLane0), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_tile_store(const uint8_t* stage, const CUtensorMap* qmap,
+                                               const CUtensorMap* kmap, int tile) {
+  const int z = tile * kTmaTileTokens;
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3}], [%4];"
+               ::"l"(qmap), "r"(kRopeLane0), "r"(0), "r"(z), "r"(smem_u32(stage))
+               : "memory");
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];"
+               ::"l"(kmap), "r"(kRopeLane0), "r"(z), "r"(smem_u32(stage + kTmaQBytes))
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+template <int S>
+__global__ void __launch_bounds__(kBlock) ceiling_tma_slices_kernel(const __grid_constant__ CUtensorMap qmap,
+                                                                    const __grid_constant__ CUtensorMap kmap,
+                                                                    int tiles, int32_t* status) {
+  extern __shared__ __align__(128) uint8_t ring[];
+  __shared__ __align__(8) uint64_t full[S];
+  const bool leader = threadIdx.x == 0;
+  if (leader) {
+    for (int s = 0; s < S; ++s) mbar_init(&full[s], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (int i = 0; i < S; ++i) {  // before the wait: L2 prefetch of the first tiles
+      const int t = blockIdx.x + i * gridDim.x;
+      if (t >= tiles) break;
+      asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];"
+                   ::"l"(&qmap), "r"(kRopeLane0), "r"(0), "r"(t * kTmaTileTokens) : "memory");
+      asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];"
+                   ::"l"(&kmap), "r"(kRopeLane0), "r"(t * kTmaTileTokens) : "memory");
+    }
+  }
+  __syncthreads();
+  pdl_enter();
+  if (!leader) return;
+  for (int i = 0; i < S; ++i) {
+    const int t = blockIdx.x + i * gridDim.x;
+    if (t >= tiles) break;
+    tma_tile_load(ring + i * kTmaStageBytes, &qmap, &kmap, t, &full[i]);
+  }
+  for (int i = 0;; ++i) {
+    const int t = blockIdx.x + i * gridDim.x;
+    if (t >= tiles) break;
+    const int s = i % S;
+    uint8_t* stage = ring + s * kTmaStageBytes;
+    bool landed = false;
+    for (int poll = 0; poll < kTmaWaitPolls && !landed; ++poll) landed = mbar_poll(&full[s], (i / S) & 1);
+    if (!landed) {
+      raise_status(status, WELM_ROPE_DEV_WAIT_TIMEOUT);
+      break;
+    }
+    tma_tile_store(stage, &qmap, &kmap, t);
+    const int next = t + S * gridDim.x;
+    if (next < tiles) {
+      asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // the stores have read the stage
+      tma_tile_load(stage, &qmap, &kmap, next, &full[s]);
+    }
+  }
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// The driver's tensor-map encoder, looked up once through the runtime.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult found;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &found) != cudaSuccess ||
+        found != cudaDriverEntryPointSuccess) {
+      cudaGetLastError();
+      return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
+    }
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }();
+  return fn;
+}
+
+// Tensor maps of Q ({256 lanes, 6 heads, N tokens}) and K ({256 lanes, N
+// tokens}) with the tile boxes above; false when the driver refuses them.
+bool encode_slice_maps(void* q, void* k, int64_t n_tokens, int64_t q_stride, int64_t k_stride, CUtensorMap& qmap,
+                       CUtensorMap& kmap) {
+  const PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  if (encode == nullptr) return false;
+  const cuuint32_t unit[3] = {1, 1, 1};
+  const cuuint64_t qdim[3] = {cuuint64_t(kHeadDim), cuuint64_t(kQHeads), cuuint64_t(n_tokens)};
+  const cuuint64_t qstride[2] = {cuuint64_t(kHeadDim) * 2, cuuint64_t(q_stride) * 2};
+  const cuuint32_t qbox[3] = {cuuint32_t(kRopeDim), cuuint32_t(kQHeads), cuuint32_t(kTmaTileTokens)};
+  const cuuint64_t kdim[2] = {cuuint64_t(kHeadDim), cuuint64_t(n_tokens)};
+  const cuuint64_t kstride[1] = {cuuint64_t(k_stride) * 2};
+  const cuuint32_t kbox[2] = {cuuint32_t(kRopeDim), cuuint32_t(kTmaTileTokens)};
+  return encode(&qmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, q, qdim, qstride, qbox, unit,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS &&
+         encode(&kmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, kdim, kstride, kbox, unit,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int S>
+int launch_tma_slices(const CUtensorMap& qmap, const CUtensorMap& kmap, int tiles, int ctas, int32_t* status,
+                      cudaStream_t stream) {
+  const size_t smem = size_t(S) * kTmaStageBytes;
+  if (cudaFuncSetAttribute(ceiling_tma_slices_kernel<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return WELM_ROPE_ERR_CUDA;
+  }
+  return launch(ceiling_tma_slices_kernel<S>, unsigned(ctas), kBlock, smem, stream, qmap, kmap, tiles, status);
+}
+
 }  // namespace
 
 extern "C" {
@@ -183,6 +351,29 @@ int welm_rope_ceiling_gather(const int64_t* positions, const float* cos_sin_cach
   const LaunchShape shape = stream_shape(items);
   return launch(ceiling_gather_kernel, shape.grid, shape.block, 0, static_cast<cudaStream_t>(stream), positions,
                 cos_sin_cache, int32_t(items), max_position, sink);
+}
+
+int welm_rope_ceiling_tma_slices(void* q, void* k, int64_t n_tokens, int64_t q_token_stride, int64_t k_token_stride,
+                                 int32_t ctas, int32_t stages, int32_t* device_status, void* stream) {
+  if (n_tokens < 0 || n_tokens > int64_t(INT32_MAX) - kTmaTileTokens || ctas < 0) return WELM_ROPE_ERR_BAD_SIZE;
+  if (stages != 2 && stages != 4 && stages != 6) return WELM_ROPE_ERR_BAD_MODE;
+  if (n_tokens == 0) return WELM_ROPE_OK;
+  if (!q || !k) return WELM_ROPE_ERR_NULL_POINTER;
+  if (q_token_stride < kQHeads * kHeadDim || k_token_stride < kHeadDim || !aligned16(q) || !aligned16(k) ||
+      q_token_stride % 8 != 0 || k_token_stride % 8 != 0)
+    return WELM_ROPE_ERR_BAD_STRIDE;  // tensor maps need 16-byte bases and strides
+  CUtensorMap qmap, kmap;
+  if (!encode_slice_maps(q, k, n_tokens, q_token_stride, k_token_stride, qmap, kmap)) return WELM_ROPE_ERR_CUDA;
+  const int tiles = int((n_tokens + kTmaTileTokens - 1) / kTmaTileTokens);
+  const int sms = current_sm_count();
+  int grid = ctas > 0 ? ctas : 2 * (sms > 0 ? sms : 1);
+  if (grid > tiles) grid = tiles;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (stages) {
+    case 2: return launch_tma_slices<2>(qmap, kmap, tiles, grid, device_status, st);
+    case 4: return launch_tma_slices<4>(qmap, kmap, tiles, grid, device_status, st);
+    default: return launch_tma_slices<6>(qmap, kmap, tiles, grid, device_status, st);
+  }
 }
 
 }  // extern "C"

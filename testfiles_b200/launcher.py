@@ -194,6 +194,24 @@ def ceiling_slices(q: torch.Tensor, k: torch.Tensor) -> None:
     _native.check("welm_rope_ceiling_slices", rc)
 
 
+def ceiling_tma_slices(q: torch.Tensor, k: torch.Tensor, ctas: int = 0, stages: int = 6,
+                       status: Optional[torch.Tensor] = None) -> None:
+    """The same slices as :func:`ceiling_slices` moved through shared memory
+    by TMA (welm_rope_ceiling_tma_slices): ``ctas`` persistent CTAs (0: two
+    per SM), a ring of ``stages`` 16-token tiles each, data unchanged."""
+    ops._check_heads(q, "query", ops.NUM_Q_HEADS)
+    ops._check_heads(k, "key", ops.NUM_K_HEADS)
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16:
+        raise TypeError("ceiling_tma_slices needs bf16 q and k")
+    if q.device != k.device or q.device.type != "cuda" or q.shape[0] != k.shape[0]:
+        raise ValueError("ceiling_tma_slices needs q and k with the same rows on one CUDA device")
+    lib = _native.load()
+    rc = ops._call(q.device, lib.welm_rope_ceiling_tma_slices, q.data_ptr(), k.data_ptr(), int(q.shape[0]),
+                   int(q.stride(0)), int(k.stride(0)), int(ctas), int(stages), ops._status_ptr(status, q.device),
+                   torch.cuda.current_stream(q.device).cuda_stream)
+    _native.check("welm_rope_ceiling_tma_slices", rc)
+
+
 def ceiling_gather(positions: torch.Tensor, cache: torch.Tensor) -> None:
     """The ordinary kernels' position and cos/sin gather alone
     (welm_rope_ceiling_gather) over ``positions``, on the current stream of
@@ -247,15 +265,36 @@ def slice_floor_us(buffers: list[tuple[torch.Tensor, torch.Tensor]], device: tor
     return us
 
 
+def tma_floor_us(buffers: list[tuple[torch.Tensor, torch.Tensor]], device: torch.device, stages: int = 6,
+                 ctas: int = 0, trials: int = 5, graph_launches: int = 64, replays: int = 20) -> float:
+    """µs per welm_rope_ceiling_tma_slices launch over the (q, k) pairs of
+    ``buffers`` in rotation, timed like :func:`slice_floor_us`; raises if a
+    barrier wait gave up."""
+    status = torch.zeros(1, dtype=torch.int32, device=device)
+    ceiling_tma_slices(*buffers[0], ctas, stages, status)
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(graph_launches):
+            ceiling_tma_slices(*buffers[i % len(buffers)], ctas, stages, status)
+    us = _replay_us(graph, device, trials, replays, graph_launches)
+    del graph
+    if int(status.item()) != 0:
+        raise RuntimeError(f"welm_rope_ceiling_tma_slices reported device status {int(status.item())}")
+    return us
+
+
 def time_case(case: workloads.Case, device: torch.device, trials: int = 5, graph_launches: int = 64,
               replays: Optional[int] = None, from_lens: bool = False, copy_ceiling: bool = False,
-              shared_cache: bool = False, sets: Optional[int] = None) -> dict:
+              shared_cache: bool = False, sets: Optional[int] = None, tma_floor: bool = False) -> dict:
     """µs per launch of ``case`` (graph-replayed over rotating buffer sets);
     ``from_lens`` runs segmented mirror cases through rope_mirror_from_lens.
     ``shared_cache`` gives every set the same cos/sin cache (hot in L2, as
     in serving) instead of a private copy each.  ``sets`` overrides the
     number of buffer sets (default: enough that more than twice the L2
-    lies between reuses, at most 64); one or two keep the data L2-resident."""
+    lies between reuses, at most 64); one or two keep the data L2-resident.
+    ``tma_floor`` (dense ordinary cases) also times the TMA-staged slice
+    mover on the same buffers, best of 2, 4 and 6 stages."""
     host = workloads.make_inputs(case, "cpu")
     nbytes = workloads.min_bytes(case)
     if sets is None:
@@ -288,6 +327,10 @@ def time_case(case: workloads.Case, device: torch.device, trials: int = 5, graph
     if copy_ceiling and not case.is_mirror and not case.is_segmented:
         floor_us = slice_floor_us([(b.query, b.key) for b in buffers], device, trials, graph_launches, replays)
         ceiling = {"slice_floor_us": round(floor_us, 3), "frac_of_slice_floor": round(floor_us / us, 4)}
+    if tma_floor and not case.is_mirror and not case.is_segmented:
+        tma = {f"{st}_stages": round(tma_floor_us([(b.query, b.key) for b in buffers], device, st, 0, trials,
+                                                  graph_launches, replays), 3) for st in (2, 4, 6)}
+        ceiling.update({"tma_slice_floor_us": min(tma.values()), "tma_slice_floor_by_stages": tma})
     del buffers
     peak, kind = measured_hbm_peak()
     gbs = nbytes / (us * 1e3)
@@ -537,7 +580,7 @@ def write_csv(records: list[dict], path: str) -> None:
 def run(cases: Iterable[workloads.Case], device: torch.device, time_it: bool, iters: int,
         out: Optional[str], from_lens: bool = False, copy_ceiling: bool = False,
         host_transport: Optional[str] = None, shared_cache: bool = False, gather_only: bool = False,
-        sets: Optional[int] = None) -> list[dict]:
+        sets: Optional[int] = None, tma_floor: bool = False) -> list[dict]:
     records = []
     sink = open(out, "a") if out else None
     try:
@@ -546,7 +589,7 @@ def run(cases: Iterable[workloads.Case], device: torch.device, time_it: bool, it
                 rec = time_host_case(case, device, host_transport)
             elif time_it:
                 rec = time_case(case, device, from_lens=from_lens, copy_ceiling=copy_ceiling,
-                                shared_cache=shared_cache, sets=sets)
+                                shared_cache=shared_cache, sets=sets, tma_floor=tma_floor)
             else:
                 rec = launch_case(case, device, iters, from_lens, gather_only)
             records.append(rec)
@@ -575,6 +618,9 @@ def main(argv: Optional[list[str]] = None) -> int:
     parser.add_argument("--sets", type=int, default=None,
                         help="with --time: rotate this many buffer sets (the copy ceilings too) instead of "
                              "enough to keep L2 cold; 1 or 2 keep every byte L2-resident")
+    parser.add_argument("--tma-floor", action="store_true",
+                        help="with --time (dense ordinary cases): also time the TMA-staged slice mover "
+                             "(welm_rope_ceiling_tma_slices) on the same buffers")
     parser.add_argument("--mirror-from-lens", action="store_true",
                         help="run segmented KV-mirror cases through rope_mirror_from_lens")
     parser.add_argument("--copy-ceiling", action="store_true",
@@ -612,7 +658,7 @@ def main(argv: Optional[list[str]] = None) -> int:
                 fh.write(json.dumps(rec) + "\n")
         return 0
     records = run(select_cases(args.cases), device, args.time, args.iters, args.json, args.mirror_from_lens,
-                  args.copy_ceiling, args.host, args.shared_cache, args.gather_only, args.sets)
+                  args.copy_ceiling, args.host, args.shared_cache, args.gather_only, args.sets, args.tma_floor)
     if args.csv:
         write_csv(records, args.csv)
     return 0

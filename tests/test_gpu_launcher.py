@@ -8,6 +8,7 @@ import json
 import pytest
 import torch
 
+import testfiles_b200 as welm
 from testfiles_b200 import launcher, workloads
 
 pytestmark = pytest.mark.gpu
@@ -90,6 +91,41 @@ def test_ceiling_kernels_copy_exactly_and_leave_slices_unchanged():
         torch.cuda.synchronize()
         assert torch.equal(q.view(torch.int16), q0.view(torch.int16)), rows
         assert torch.equal(k.view(torch.int16), k0.view(torch.int16)), rows
+
+
+@pytest.mark.parametrize("rows,fused,ctas,stages", [(16384, False, 0, 6), (1000, True, 148, 4), (7, False, 5, 2),
+                                                    (1000, False, 3, 2), (3001, True, 0, 6)])
+def test_tma_ceiling_leaves_slices_and_neighbours_unchanged(rows, fused, ctas, stages):
+    """The TMA-staged mover rewrites the rope slices with themselves; rows
+    past N (outside its tensor maps) and the other lanes stay untouched, and
+    no barrier wait gives up."""
+    g = torch.Generator(device=DEV).manual_seed(rows + stages)
+    extra = 40
+    if fused:
+        qkv = torch.randn((rows + extra, 8 * 256), device=DEV, generator=g).to(torch.bfloat16)
+        q, k = qkv[:rows, :1536].view(rows, 6, 256), qkv[:rows, 1536:1792].view(rows, 1, 256)
+        stores = [qkv]
+    else:
+        qb = torch.randn((rows + extra, 6, 256), device=DEV, generator=g).to(torch.bfloat16)
+        kb = torch.randn((rows + extra, 1, 256), device=DEV, generator=g).to(torch.bfloat16)
+        q, k = qb[:rows], kb[:rows]
+        stores = [qb, kb]
+    before = [t.clone() for t in stores]
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    launcher.ceiling_tma_slices(q, k, ctas, stages, status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    for t, t0 in zip(stores, before):
+        assert torch.equal(t.view(torch.int16), t0.view(torch.int16))
+    with pytest.raises(welm.WelmRopeError):
+        launcher.ceiling_tma_slices(q, k, ctas, 3)
+
+
+def test_tma_floor_timing():
+    bufs = [(torch.randn((4096, 6, 256), device=DEV).to(torch.bfloat16),
+             torch.randn((4096, 1, 256), device=DEV).to(torch.bfloat16)) for _ in range(2)]
+    us = launcher.tma_floor_us(bufs, DEV, stages=4, trials=2, graph_launches=8, replays=2)
+    assert 0.0 < us < 1000.0
 
 
 def test_gather_ceiling_reads_without_writing():

@@ -309,6 +309,22 @@ def test_ceiling_entries_host_validation():
     assert gather(None, None, 0, 64, None, None) == _native.OK
     assert gather(None, FAKE, 4, 64, None, None) == _native.ERR_NULL_POINTER
     assert gather(FAKE, FAKE + 8, 4, 64, None, None) == _native.ERR_BAD_STRIDE  # the cache is read in 16-byte vectors
+    tma = lib.welm_rope_ceiling_tma_slices
+    assert tma(FAKE, FAKE, -1, 1536, 256, 0, 4, None, None) == _native.ERR_BAD_SIZE
+    assert tma(FAKE, FAKE, 1 << 31, 1536, 256, 0, 4, None, None) == _native.ERR_BAD_SIZE
+    assert tma(FAKE, FAKE, 4, 1536, 256, -1, 4, None, None) == _native.ERR_BAD_SIZE
+    assert tma(FAKE, FAKE, 4, 1536, 256, 0, 3, None, None) == _native.ERR_BAD_MODE  # 2, 4 or 6 stages
+    assert tma(None, None, 0, 0, 0, 0, 2, None, None) == _native.OK
+    assert tma(None, FAKE, 4, 1536, 256, 0, 2, None, None) == _native.ERR_NULL_POINTER
+    assert tma(FAKE, FAKE, 1, 0, 0, 0, 2, None, None) == _native.ERR_BAD_STRIDE  # tensor maps need whole rows
+    assert tma(FAKE, FAKE, 4, 1540, 256, 0, 2, None, None) == _native.ERR_BAD_STRIDE
+    assert tma(FAKE + 8, FAKE, 4, 1536, 256, 0, 2, None, None) == _native.ERR_BAD_STRIDE
+
+
+def test_device_status_bits_match_the_header():
+    header = (REPO / "include" / "welm_rope.h").read_text()
+    bits = {m.group(1): int(m.group(2)) for m in re.finditer(r"#define WELM_ROPE_DEV_(\w+) (\d+)", header)}
+    assert bits == {name[len("DEV_"):]: getattr(_native, name) for name in dir(_native) if name.startswith("DEV_")}
 
 
 def test_launcher_rejects_fewer_than_one_buffer_set():
