@@ -88,3 +88,44 @@ def test_sharded_outputs_concatenate_to_the_golden_digests():
             ks.append(k)
         assert bench.sha256_rows(torch.cat(qs)) == want["query"], world
         assert bench.sha256_rows(torch.cat(ks)) == want["key"], world
+
+
+def _rank_helpers_worker(rank: int, world: int, port: int, queue) -> None:
+    import os
+
+    import torch
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        bench = load_bench()
+        own = 5.0 + rank  # each rank's own timing
+        top = bench.max_over_ranks(dist, own, torch.device("cpu"))
+        every = bench.all_ranks(dist, own, torch.device("cpu"))
+        queue.put((rank, top, every))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_rank_timing_helpers_over_two_gloo_ranks():
+    """The max over ranks and every rank's own value, as the bench's timed
+    legs report them, are the same on both ranks of a world_size-2 group."""
+    import socket
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    procs = [ctx.Process(target=_rank_helpers_worker, args=(r, 2, port, queue)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = sorted(queue.get(timeout=240) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert results == [(0, 6.0, [5.0, 6.0]), (1, 6.0, [5.0, 6.0])]
+    assert load_bench().all_ranks(None, 3.5, None) == [3.5]
